@@ -1,0 +1,356 @@
+// Paged-KV decode attention (one query token per sequence, GQA).
+//
+// Work decomposition: one CTA per (context split, kv head, sequence).  A
+// dedicated producer warp streams 64-token K and V tiles of the split from
+// the paged pool into a STAGES-deep shared-memory ring with TMA tensor copies
+// (128-byte swizzle, completion on mbarriers).  Four consumer warps each own
+// 16 tokens of every tile and compute S = Q K^T and O += P V with
+// mma.sync m16n8k16 (the G query heads that share the kv head are the rows of
+// the A operand), keeping an online softmax in fp32.  The four partial
+// (max, sum, O) triples are merged in shared memory; a split either writes
+// the final bf16 output (single split) or an fp32 partial that
+// decode_combine_kernel merges.
+//
+// The kernel is HBM-bound: each K/V byte of the context is read once per
+// kv head.  Algorithmic bytes per call = sum(ctx) * Hkv * 128 * 2 * 2.
+#include "common.cuh"
+#include "host.h"
+
+namespace aacc {
+
+constexpr int kD = 128;
+constexpr int kTile = 64;
+constexpr int kConsumerWarps = 4;
+constexpr int kDecodeThreads = (kConsumerWarps + 1) * 32;
+constexpr int kDecodeStages = 3;
+constexpr int kHalfTileBytes = kTile * 64 * 2;  // 64 rows x 64 dims bf16 = 8 KB
+
+struct DecodeSmem {
+  // [stage][K half0, K half1, V half0, V half1], each 8 KB, 1024-aligned.
+  bf16 tiles[kDecodeStages][4][kTile * 64];
+  uint64_t full[kDecodeStages];
+  uint64_t empty[kDecodeStages];
+  float red_m[kConsumerWarps][8];
+  float red_l[kConsumerWarps][8];
+  int abort;
+};
+
+template <int G>
+__global__ void __launch_bounds__(kDecodeThreads, 2)
+    paged_decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                        const bf16* __restrict__ q, bf16* __restrict__ out, float* __restrict__ ws_o,
+                        float* __restrict__ ws_ml, const int32_t* __restrict__ bt, int64_t max_blocks,
+                        const int64_t* __restrict__ rows, const int32_t* __restrict__ seqlens, int ctx_add,
+                        int Hkv, int bs, int64_t num_blocks, int64_t max_ctx, int split_tokens, int max_splits,
+                        float scale_log2, unsigned* err) {
+  extern __shared__ uint8_t smem_raw[];
+  DecodeSmem& sm = *reinterpret_cast<DecodeSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  const int s = blockIdx.x, h = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int Hq = Hkv * G;
+  const int64_t row = rows[b];
+  int64_t ctx = (int64_t)seqlens[row] + ctx_add;
+  if (ctx > max_ctx) {  // max_ctx <= max_blocks * bs and <= max_splits * split_tokens
+    if (threadIdx.x == 0 && s == 0) report(err, ERR_CTX_OOB);
+    ctx = max_ctx;
+  }
+  if (ctx <= 0) {
+    // Nothing to attend to: define the output as zeros.
+    if (s == 0)
+      for (int i = threadIdx.x; i < G * kD; i += blockDim.x)
+        out[(b * Hq + (int64_t)h * G) * kD + i] = tobf(0.f);
+    return;
+  }
+  const int n_splits = (int)((ctx + split_tokens - 1) / split_tokens);
+  if (s >= n_splits) return;
+  const int64_t t_begin = (int64_t)s * split_tokens;
+  const int64_t t_end = min(t_begin + split_tokens, ctx);
+  const int ntiles = (int)((t_end - t_begin + kTile - 1) / kTile);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kDecodeStages; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], kConsumerWarps);
+    }
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  volatile int* abort = &sm.abort;
+
+  if (warp == kConsumerWarps) {
+    // ---------------- producer warp ----------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tmk);
+      tma_prefetch_desc(&tmv);
+      const int32_t* btrow = bt + row * max_blocks;
+      int issued = 0;
+      for (int i = 0; i < ntiles; ++i) {
+        const int st = i % kDecodeStages;
+        if (i >= kDecodeStages && !mbar_wait(&sm.empty[st], ((i / kDecodeStages) - 1) & 1, err, abort)) break;
+        const int64_t t0 = t_begin + (int64_t)i * kTile;
+        int64_t blk = btrow[t0 / bs];
+        if (blk < 0 || blk >= num_blocks) {
+          report(err, ERR_BLOCK_OOB);
+          blk = 0;  // keep the pipeline moving on a valid address; the result is flagged
+        }
+        const int r = (int)((blk * Hkv + h) * bs + t0 % bs);
+        mbar_arrive_expect_tx(&sm.full[st], 4 * kHalfTileBytes);
+        tma_load_2d(sm.tiles[st][0], &tmk, &sm.full[st], 0, r);
+        tma_load_2d(sm.tiles[st][1], &tmk, &sm.full[st], 64, r);
+        tma_load_2d(sm.tiles[st][2], &tmv, &sm.full[st], 0, r);
+        tma_load_2d(sm.tiles[st][3], &tmv, &sm.full[st], 64, r);
+        ++issued;
+      }
+      // Drain: every copy this CTA issued has landed before the CTA may exit.
+      for (int st = 0; st < kDecodeStages && st < issued; ++st) {
+        const int last = st + ((issued - 1 - st) / kDecodeStages) * kDecodeStages;
+        mbar_wait(&sm.full[st], (last / kDecodeStages) & 1, err, nullptr);
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumer warps ----------------
+  const int g = lane >> 2, c = lane & 3;
+  // Q as the A operand: rows = the G query heads of this kv head (rows >= G are zero).
+  uint32_t qa[8][4];
+  {
+    const bf16* qrow = q + (b * Hq + (int64_t)h * G + (g < G ? g : 0)) * kD;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      uint32_t lo = 0, hi = 0;
+      if (g < G) {
+        lo = *reinterpret_cast<const uint32_t*>(qrow + 16 * kk + 2 * c);
+        hi = *reinterpret_cast<const uint32_t*>(qrow + 16 * kk + 2 * c + 8);
+      }
+      qa[kk][0] = lo;
+      qa[kk][1] = 0;
+      qa[kk][2] = hi;
+      qa[kk][3] = 0;
+    }
+  }
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;
+
+  const int mi = lane >> 3, r8 = lane & 7;
+  const int ktok = 16 * warp + (mi >> 1) * 8 + r8;  // K ldmatrix row (token within tile)
+  const int vtok = 16 * warp + (mi & 1) * 8 + r8;   // V ldmatrix row
+  bool ok = true;
+  for (int i = 0; i < ntiles; ++i) {
+    const int st = i % kDecodeStages;
+    if (!mbar_wait(&sm.full[st], (i / kDecodeStages) & 1, err, abort)) {
+      ok = false;
+      break;
+    }
+    const uint32_t kb = smem_u32(sm.tiles[st][0]);
+    const uint32_t vb = smem_u32(sm.tiles[st][2]);
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int chunk = 2 * kk + (mi & 1);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(kb + (chunk >> 3) * kHalfTileBytes + swz128(ktok, chunk & 7), b0, b1, b2, b3);
+      mma_bf16_16816(sc[0], qa[kk], b0, b1);
+      mma_bf16_16816(sc[1], qa[kk], b2, b3);
+    }
+    const int64_t tbase = t_begin + (int64_t)i * kTile + 16 * warp + 2 * c;
+    float x[4];
+    x[0] = (tbase + 0 < t_end) ? sc[0][0] * scale_log2 : -INFINITY;
+    x[1] = (tbase + 1 < t_end) ? sc[0][1] * scale_log2 : -INFINITY;
+    x[2] = (tbase + 8 < t_end) ? sc[1][0] * scale_log2 : -INFINITY;
+    x[3] = (tbase + 9 < t_end) ? sc[1][1] * scale_log2 : -INFINITY;
+    float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m_run, mx);
+    const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+    const float alpha = exp2f(m_run - m_use);
+    float p[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) p[j] = exp2f(x[j] - m_use);
+    l_run = l_run * alpha + (p[0] + p[1] + p[2] + p[3]);
+    m_run = m_new;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      o[j][0] *= alpha;
+      o[j][1] *= alpha;
+    }
+    uint32_t pa[4];
+    pa[0] = pack_bf16(p[0], p[1]);
+    pa[1] = 0;
+    pa[2] = pack_bf16(p[2], p[3]);
+    pa[3] = 0;
+#pragma unroll
+    for (int jp = 0; jp < 8; ++jp) {
+      const int chunk = 2 * jp + (mi >> 1);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(vb + (chunk >> 3) * kHalfTileBytes + swz128(vtok, chunk & 7), b0, b1, b2, b3);
+      mma_bf16_16816(o[2 * jp], pa, b0, b1);
+      mma_bf16_16816(o[2 * jp + 1], pa, b2, b3);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty[st]);
+  }
+  // Quad-reduce the row sum (all four lanes of a quad hold the same running max).
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+
+  // Merge the four consumer warps through shared memory (reusing the tile ring).
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32));
+  float* red_o = reinterpret_cast<float*>(&sm.tiles[0][0][0]);  // [warp][G][128]
+  if (g < G) {
+    if (c == 0) {
+      sm.red_m[warp][g] = ok ? m_run : -INFINITY;
+      sm.red_l[warp][g] = ok ? l_run : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      red_o[(warp * G + g) * kD + 8 * j + 2 * c] = o[j][0];
+      red_o[(warp * G + g) * kD + 8 * j + 2 * c + 1] = o[j][1];
+    }
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32));
+  const int d = threadIdx.x;  // 0..127
+#pragma unroll
+  for (int gg = 0; gg < G; ++gg) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm.red_m[w][gg]);
+    const float Mu = (M == -INFINITY) ? 0.f : M;
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      const float f = exp2f(sm.red_m[w][gg] - Mu);
+      L += f * sm.red_l[w][gg];
+      O += f * red_o[(w * G + gg) * kD + d];
+    }
+    const int64_t qh = b * Hq + (int64_t)h * G + gg;
+    if (n_splits == 1) {
+      out[qh * kD + d] = tobf(L > 0.f ? O / L : 0.f);
+    } else {
+      ws_o[(qh * max_splits + s) * kD + d] = O;
+      if (d == 0) {
+        ws_ml[(qh * max_splits + s) * 2 + 0] = M;
+        ws_ml[(qh * max_splits + s) * 2 + 1] = L;
+      }
+    }
+  }
+}
+
+// Merge the per-split partials of rows whose context needed more than one split.
+__global__ void decode_combine_kernel(bf16* __restrict__ out, const float* __restrict__ ws_o,
+                                      const float* __restrict__ ws_ml, const int64_t* __restrict__ rows,
+                                      const int32_t* __restrict__ seqlens, int ctx_add, int Hq, int64_t max_ctx,
+                                      int split_tokens, int max_splits) {
+  const int hq = blockIdx.x;
+  const int64_t b = blockIdx.y;
+  int64_t ctx = (int64_t)seqlens[rows[b]] + ctx_add;
+  if (ctx > max_ctx) ctx = max_ctx;
+  const int n_splits = (int)((ctx + split_tokens - 1) / split_tokens);
+  if (n_splits <= 1) return;
+  const int64_t qh = b * Hq + hq;
+  const int d = threadIdx.x;
+  float M = -INFINITY;
+  for (int s = 0; s < n_splits; ++s) M = fmaxf(M, ws_ml[(qh * max_splits + s) * 2]);
+  const float Mu = (M == -INFINITY) ? 0.f : M;
+  float L = 0.f, O = 0.f;
+  for (int s = 0; s < n_splits; ++s) {
+    const float f = exp2f(ws_ml[(qh * max_splits + s) * 2] - Mu);
+    L += f * ws_ml[(qh * max_splits + s) * 2 + 1];
+    O += f * ws_o[(qh * max_splits + s) * kD + d];
+  }
+  out[qh * kD + d] = tobf(L > 0.f ? O / L : 0.f);
+}
+
+static int default_split(int64_t batch, int Hkv, int64_t max_ctx) {
+  const int64_t target = 148 * 8;  // CTAs to keep every SM busy (two resident, several waves)
+  int64_t want = (target + batch * Hkv - 1) / (batch * Hkv);
+  int64_t split = (max_ctx + want - 1) / want;
+  split = ((split + kTile - 1) / kTile) * kTile;
+  if (split < kTile) split = kTile;
+  if (split > 512) split = 512;
+  return (int)split;
+}
+
+static size_t decode_smem_bytes() { return sizeof(DecodeSmem) + 1024; }
+
+}  // namespace aacc
+
+using namespace aacc;
+
+extern "C" {
+
+int64_t aacc_paged_decode_workspace_bytes(int64_t batch, int num_q_heads, int64_t max_context, int split_tokens) {
+  if (split_tokens <= 0) split_tokens = default_split(batch, 1, max_context);  // upper bound on splits
+  int64_t max_splits = (max_context + split_tokens - 1) / split_tokens;
+  if (max_splits < 1) max_splits = 1;
+  return batch * num_q_heads * max_splits * (kD + 2) * (int64_t)sizeof(float);
+}
+
+int aacc_paged_decode_attention(const void* q, void* out, const void* k_cache, const void* v_cache, int64_t num_blocks,
+                                const int32_t* block_tables, int64_t max_blocks, const int64_t* slot_indices,
+                                const int32_t* seqlens, int ctx_add, int64_t batch, int num_q_heads,
+                                int num_kv_heads, int block_size, float scale, int split_tokens,
+                                int64_t max_context, void* workspace, int64_t workspace_bytes,
+                                cudaStream_t stream) {
+  if (batch < 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads || block_size <= 0 || block_size % kTile ||
+      num_blocks <= 0 || max_blocks <= 0 || max_context <= 0)
+    return set_error(AACC_ERR_INVALID, "paged_decode_attention: bad sizes");
+  if (batch == 0) return AACC_OK;
+  const int G = num_q_heads / num_kv_heads;
+  if (G != 1 && G != 2 && G != 4 && G != 8)
+    return set_error(AACC_ERR_UNSUPPORTED, "paged_decode_attention: q/kv head ratio %d not in {1,2,4,8}", G);
+  if (max_context > max_blocks * block_size) max_context = max_blocks * block_size;
+  const int64_t rows = num_blocks * num_kv_heads * block_size;
+  if (rows >= (int64_t(1) << 31)) return set_error(AACC_ERR_UNSUPPORTED, "paged_decode_attention: pool too large");
+  if (split_tokens <= 0) split_tokens = default_split(batch, num_kv_heads, max_context);
+  if (split_tokens % kTile) return set_error(AACC_ERR_INVALID, "split_tokens must be a multiple of %d", kTile);
+  const int max_splits = (int)((max_context + split_tokens - 1) / split_tokens);
+  if (max_splits > 1) {
+    const int64_t need = batch * num_q_heads * (int64_t)max_splits * (kD + 2) * (int64_t)sizeof(float);
+    if (!workspace || workspace_bytes < need)
+      return set_error(AACC_ERR_INVALID, "paged_decode_attention: workspace %lld < %lld bytes",
+                       (long long)workspace_bytes, (long long)need);
+  }
+  CUtensorMap tmk, tmv;
+  int st = make_tmap_2d(&tmk, k_cache, kD, rows, kD * 2, 64, kTile, true);
+  if (st) return st;
+  st = make_tmap_2d(&tmv, v_cache, kD, rows, kD * 2, 64, kTile, true);
+  if (st) return st;
+  float* ws_o = static_cast<float*>(workspace);
+  float* ws_ml = ws_o ? ws_o + batch * num_q_heads * (int64_t)max_splits * kD : nullptr;
+  const float scale_log2 = scale * kLog2e;
+  unsigned* err = device_error_ptr();
+  dim3 grid(max_splits, num_kv_heads, (unsigned)batch);
+  const size_t smem = decode_smem_bytes();
+#define AACC_LAUNCH_DECODE(GG)                                                                                   \
+  {                                                                                                              \
+    auto kern = paged_decode_kernel<GG>;                                                                         \
+    set_smem_once<paged_decode_kernel<GG>>((int)smem);                                                           \
+    kern<<<grid, kDecodeThreads, smem, stream>>>(tmk, tmv, (const bf16*)q, (bf16*)out, ws_o, ws_ml, block_tables, \
+                                                 max_blocks, slot_indices, seqlens, ctx_add, num_kv_heads,       \
+                                                 block_size, num_blocks, max_context, split_tokens, max_splits, scale_log2, err); \
+  }
+  switch (G) {
+    case 1: AACC_LAUNCH_DECODE(1) break;
+    case 2: AACC_LAUNCH_DECODE(2) break;
+    case 4: AACC_LAUNCH_DECODE(4) break;
+    default: AACC_LAUNCH_DECODE(8) break;
+  }
+#undef AACC_LAUNCH_DECODE
+  st = check_launch("paged_decode_kernel");
+  if (st) return st;
+  if (max_splits > 1) {
+    decode_combine_kernel<<<dim3(num_q_heads, (unsigned)batch), kD, 0, stream>>>(
+        (bf16*)out, ws_o, ws_ml, slot_indices, seqlens, ctx_add, num_q_heads, max_context, split_tokens, max_splits);
+    st = check_launch("decode_combine_kernel");
+  }
+  return st;
+}
+
+}  // extern "C"

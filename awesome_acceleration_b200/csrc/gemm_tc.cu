@@ -1,0 +1,546 @@
+// tcgen05 / TMEM GEMMs with fused epilogues for the Qwen3 projections.
+//
+//   out = x @ w^T,  x: [M][K] activations (A, K-major), w: [N][K] weights
+//   (B, K-major, the nn.Linear layout).
+//
+// One CTA computes an (MT*128) x BN output tile.  Warp 0 (one elected lane)
+// streams 64-wide K slabs of A and B into a STAGES-deep ring with TMA
+// (128-byte swizzle); warp 1 (one lane) issues tcgen05.mma (M=128, N=BN,
+// K=16, bf16 in / fp32 accumulate) into TMEM, releasing ring slots with
+// tcgen05.commit; warp 2 owns the TMEM allocation.  After the last slab all
+// eight warps drain TMEM with tcgen05.ld (warp w reads TMEM lanes
+// 32*(w%4)..+31, i.e. one output row per thread) and run the epilogue:
+//
+//   EPI_STORE   bf16(acc)
+//   EPI_SILU    bf16(silu(bf16(gate))) * bf16(up) on interleaved gate/up rows
+//   EPI_QKV     per-head RMSNorm (q_norm / k_norm) + RoPE for Q/K heads, then
+//               Q to q_out and K/V rows straight into the paged KV cache
+//   EPI_ARGMAX  per-row (max, first index) of bf16(acc) over each 128-column
+//               group (lm_head + greedy sampling without materialised logits)
+//
+// Decode batches (M <= 256) are weight-bandwidth bound: every weight byte is
+// read once (MT=2 keeps both 128-row halves of the batch in one CTA);
+// prefill tiles (MT=2, BN=256) are tensor-pipe bound.
+#include "common.cuh"
+#include "host.h"
+
+namespace aacc {
+
+enum Epi { EPI_STORE = 0, EPI_SILU = 1, EPI_QKV = 2, EPI_ARGMAX = 3 };
+
+struct EpiParams {
+  bf16* out;
+  int64_t ldo;
+  // EPI_QKV
+  const bf16* qn_w;
+  const bf16* kn_w;
+  float eps;
+  const int64_t* positions;
+  const bf16* rope;  // [max_pos][128] = cos[64] | sin[64]
+  int64_t max_pos;
+  const int64_t* slot_mapping;
+  bf16* k_cache;
+  bf16* v_cache;
+  int64_t num_slots;
+  int Hq, Hkv, bs;
+  // EPI_ARGMAX
+  float* part_val;
+  int32_t* part_idx;
+  int64_t n_groups;
+  unsigned* err;
+};
+
+constexpr int kGemmThreads = 256;
+
+template <int BN, int MT>
+struct GemmCfg {
+  static constexpr int A_BYTES = MT * 128 * 128;  // MT*128 rows x 64 bf16
+  static constexpr int B_BYTES = BN * 128;        // BN rows x 64 bf16
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  static constexpr int TMEM_COLS = MT * BN;  // 128, 256 or 512
+  static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 + 256;
+};
+
+// ---- tcgen05 wrappers ------------------------------------------------------
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  // K-major, 128-byte swizzle: 8-row core groups 1024 bytes apart (SBO),
+  // leading offset unused (1), descriptor version 1, layout SWIZZLE_128B (2).
+  return (uint64_t)((saddr & 0x3FFFF) >> 4) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
+         (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+template <int BN>
+__device__ __forceinline__ constexpr uint32_t umma_idesc_bf16() {
+  // D fp32 (bit 4), A bf16 (bits 7-9 = 1), B bf16 (bits 10-12 = 1), both
+  // K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28 (M = 128).
+  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(128 >> 4) << 24);
+}
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void store16_bf16(bf16* dst, const float (&v)[16]) {
+  uint4 a, b;
+  a.x = pack_bf16(v[0], v[1]);
+  a.y = pack_bf16(v[2], v[3]);
+  a.z = pack_bf16(v[4], v[5]);
+  a.w = pack_bf16(v[6], v[7]);
+  b.x = pack_bf16(v[8], v[9]);
+  b.y = pack_bf16(v[10], v[11]);
+  b.z = pack_bf16(v[12], v[13]);
+  b.w = pack_bf16(v[14], v[15]);
+  reinterpret_cast<uint4*>(dst)[0] = a;
+  reinterpret_cast<uint4*>(dst)[1] = b;
+}
+__device__ __forceinline__ void load16_bf16(const bf16* src, float (&v)[16]) {
+  uint4 a = reinterpret_cast<const uint4*>(src)[0], b = reinterpret_cast<const uint4*>(src)[1];
+  const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
+  const uint32_t* pb = reinterpret_cast<const uint32_t*>(&b);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float2 f = unpack_bf16(pa[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+    f = unpack_bf16(pb[j]);
+    v[8 + 2 * j] = f.x;
+    v[8 + 2 * j + 1] = f.y;
+  }
+}
+
+// ---- epilogues: one thread = one output row, 128 columns ------------------
+// `tcol` is the TMEM address of column 0 of this 128-column group for this
+// warp's lane quarter; `n0` the global column of that column 0.
+template <int EPI>
+__device__ __forceinline__ void epilogue_group(uint32_t tcol, int64_t m, bool row_ok, int64_t n0, int64_t N,
+                                               const EpiParams& p) {
+  if constexpr (EPI == EPI_STORE) {
+#pragma unroll 1
+    for (int c = 0; c < 128; c += 16) {
+      float v[16];
+      tmem_ld16(tcol + c, v);
+      if (row_ok) {
+        if (n0 + c + 16 <= N) {
+          store16_bf16(p.out + m * p.ldo + n0 + c, v);
+        } else {
+          for (int i = 0; i < 16; ++i)
+            if (n0 + c + i < N) p.out[m * p.ldo + n0 + c + i] = tobf(v[i]);
+        }
+      }
+    }
+  } else if constexpr (EPI == EPI_SILU) {
+    const int64_t ob = n0 / 2;  // output column of gate column n0
+#pragma unroll 1
+    for (int c = 0; c < 64; c += 16) {
+      float gv[16], uv[16];
+      tmem_ld16(tcol + c, gv);
+      tmem_ld16(tcol + 64 + c, uv);
+      if (row_ok && n0 + 128 <= N) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float gg = rbf(gv[i]);
+          const float act = rbf(gg / (1.0f + expf(-gg)));
+          gv[i] = act * rbf(uv[i]);
+        }
+        store16_bf16(p.out + m * p.ldo + ob + c, gv);
+      }
+    }
+  } else if constexpr (EPI == EPI_QKV) {
+    const int hh = (int)(n0 / 128);
+    const bool is_q = hh < p.Hq, is_k = !is_q && hh < p.Hq + p.Hkv;
+    bf16* dst = nullptr;
+    if (row_ok) {
+      if (is_q) {
+        dst = p.out + m * p.ldo + (int64_t)hh * 128;
+      } else {
+        const int64_t slot = p.slot_mapping[m];
+        if (slot >= p.num_slots) report(p.err, ERR_SLOT_OOB);
+        if (slot >= 0 && slot < p.num_slots) {
+          const int kvh = is_k ? hh - p.Hq : hh - p.Hq - p.Hkv;
+          const int64_t off = ((slot / p.bs) * p.Hkv + kvh) * p.bs + slot % p.bs;
+          dst = (is_k ? p.k_cache : p.v_cache) + off * 128;
+        }
+      }
+    }
+    if (!is_q && !is_k) {  // V head: plain store
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 16) {
+        float v[16];
+        tmem_ld16(tcol + c, v);
+        if (dst) store16_bf16(dst + c, v);
+      }
+      return;
+    }
+    // Pass 1: sum of squares of the bf16-rounded projection.
+    float ss = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 128; c += 16) {
+      float v[16];
+      tmem_ld16(tcol + c, v);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float x = rbf(v[i]);
+        ss += x * x;
+      }
+    }
+    const float r = rsqrtf(ss / 128.f + p.eps);
+    const bf16* nw = is_q ? p.qn_w : p.kn_w;
+    int64_t pos = row_ok ? p.positions[m] : 0;
+    if (pos < 0 || pos >= p.max_pos) {
+      if (row_ok) report(p.err, ERR_POS_OOB);
+      pos = 0;
+    }
+    const bf16* cs = p.rope + pos * 128;
+    // Pass 2: normalise, weight, rotate (pairs i and i+64), store.
+#pragma unroll 1
+    for (int c = 0; c < 64; c += 16) {
+      float x1[16], x2[16], w1[16], w2[16], cv[16], sv[16];
+      tmem_ld16(tcol + c, x1);
+      tmem_ld16(tcol + 64 + c, x2);
+      load16_bf16(nw + c, w1);
+      load16_bf16(nw + 64 + c, w2);
+      load16_bf16(cs + c, cv);
+      load16_bf16(cs + 64 + c, sv);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float y1 = rbf(w1[i] * rbf(rbf(x1[i]) * r));
+        const float y2 = rbf(w2[i] * rbf(rbf(x2[i]) * r));
+        x1[i] = rbf(y1 * cv[i]) + rbf(-y2 * sv[i]);
+        x2[i] = rbf(y2 * cv[i]) + rbf(y1 * sv[i]);
+      }
+      if (dst) {
+        store16_bf16(dst + c, x1);
+        store16_bf16(dst + 64 + c, x2);
+      }
+    }
+  } else {  // EPI_ARGMAX
+    float best = -INFINITY;
+    int32_t bi = 0x7fffffff;
+#pragma unroll 1
+    for (int c = 0; c < 128; c += 16) {
+      float v[16];
+      tmem_ld16(tcol + c, v);
+      if (row_ok) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int64_t n = n0 + c + i;
+          const float x = rbf(v[i]);
+          if (n < N && x > best) {
+            best = x;
+            bi = (int32_t)n;
+          }
+        }
+        if (p.out) {
+          if (n0 + c + 16 <= N) {
+            store16_bf16(p.out + m * p.ldo + n0 + c, v);
+          } else {
+            for (int i = 0; i < 16; ++i)
+              if (n0 + c + i < N) p.out[m * p.ldo + n0 + c + i] = tobf(v[i]);
+          }
+        }
+      }
+    }
+    if (row_ok) {
+      const int64_t gidx = n0 / 128;
+      p.part_val[m * p.n_groups + gidx] = best;
+      p.part_idx[m * p.n_groups + gidx] = bi;
+    }
+  }
+}
+
+template <int BN, int MT, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb, int64_t M,
+                   int64_t N, int K, EpiParams p) {
+  using C = GemmCfg<BN, MT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* a_ring = base;
+  uint8_t* b_ring = base + C::STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* accum = empty + C::STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t m0 = (int64_t)blockIdx.y * (128 * MT);
+  const int64_t n_base = (int64_t)blockIdx.x * BN;
+  const int nk = K / 64;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(accum, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"((uint32_t)C::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  volatile int* abort = abort_flag;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    tma_prefetch_desc(&tma);
+    tma_prefetch_desc(&tmb);
+    const uint64_t pol_a = policy_evict_last(), pol_b = policy_evict_first();
+    int issued = 0;
+    for (int kb = 0; kb < nk; ++kb) {
+      const int st = kb % C::STAGES;
+      if (kb >= C::STAGES && !mbar_wait(&empty[st], ((kb / C::STAGES) - 1) & 1, p.err, abort)) break;
+      mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
+      tma_load_2d_hint(a_ring + st * C::A_BYTES, &tma, &full[st], kb * 64, (int)m0, pol_a);
+      tma_load_2d_hint(b_ring + st * C::B_BYTES, &tmb, &full[st], kb * 64, (int)n_base, pol_b);
+      ++issued;
+    }
+    for (int st = 0; st < C::STAGES && st < issued; ++st) {
+      const int last = st + ((issued - 1 - st) / C::STAGES) * C::STAGES;
+      mbar_wait(&full[st], (last / C::STAGES) & 1, p.err, nullptr);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    constexpr uint32_t idesc = umma_idesc_bf16<BN>();
+    for (int kb = 0; kb < nk; ++kb) {
+      const int st = kb % C::STAGES;
+      if (!mbar_wait(&full[st], (kb / C::STAGES) & 1, p.err, abort)) break;
+      tc_fence_after();
+      const uint32_t a_addr = smem_u32(a_ring + st * C::A_BYTES);
+      const uint32_t b_addr = smem_u32(b_ring + st * C::B_BYTES);
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          umma_bf16(tmem + mt * BN, umma_desc_sw128(a_addr + mt * 128 * 128 + kk * 32),
+                    umma_desc_sw128(b_addr + kk * 32), idesc, (kb | kk) != 0);
+        }
+      }
+      umma_commit(&empty[st]);
+    }
+    umma_commit(accum);  // fires once every MMA issued above has completed
+  }
+
+  // ---------------- epilogue: all eight warps ----------------
+  __syncwarp();
+  const bool have = mbar_wait(accum, 0, p.err, nullptr);
+  tc_fence_after();
+  const int quarter = warp & 3, wset = warp >> 2;
+  const int mt = (MT == 2) ? wset : 0;
+  const int64_t m = m0 + mt * 128 + quarter * 32 + lane;
+  const bool row_ok = have && !*abort && m < M;
+  const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + mt * BN;
+#pragma unroll 1
+  for (int g = 0; g < BN / 128; ++g) {
+    if (MT == 1 && (g & 1) != wset) continue;
+    epilogue_group<EPI>(trow + g * 128, m, row_ok, n_base + g * 128, N, p);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::TMEM_COLS) : "memory");
+  }
+}
+
+// Merge per-group argmax partials: highest value wins, first index on ties.
+__global__ void argmax_merge_groups_kernel(const float* __restrict__ pv, const int32_t* __restrict__ pi,
+                                           int64_t n_groups, int64_t vocab_offset, int64_t* __restrict__ tokens,
+                                           float* __restrict__ best_val) {
+  const int64_t m = blockIdx.x;
+  float best = -INFINITY;
+  int32_t bi = 0x7fffffff;
+  for (int64_t gi = threadIdx.x; gi < n_groups; gi += blockDim.x) {
+    const float v = pv[m * n_groups + gi];
+    const int32_t i = pi[m * n_groups + gi];
+    if (v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float v = __shfl_xor_sync(0xffffffffu, best, o);
+    const int32_t i = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  }
+  __shared__ float sv[32];
+  __shared__ int32_t si[32];
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    sv[w] = best;
+    si[w] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int k = 1; k < (int)(blockDim.x >> 5); ++k)
+      if (sv[k] > best || (sv[k] == best && si[k] < bi)) {
+        best = sv[k];
+        bi = si[k];
+      }
+    tokens[m] = (bi == 0x7fffffff ? 0 : bi) + vocab_offset;
+    if (best_val) best_val[m] = best;
+  }
+}
+
+// ---- host launch --------------------------------------------------------------
+template <int BN, int MT, int EPI>
+static int launch_gemm(const void* x, const void* w, int64_t M, int64_t N, int64_t K, const EpiParams& p,
+                       cudaStream_t stream) {
+  using C = GemmCfg<BN, MT>;
+  CUtensorMap ta, tb;
+  int st = make_tmap_2d(&ta, x, K, M, K * 2, 64, 128 * MT, true);
+  if (st) return st;
+  st = make_tmap_2d(&tb, w, K, N, K * 2, 64, BN, true);
+  if (st) return st;
+  auto kern = gemm_tc_kernel<BN, MT, EPI>;
+  set_smem_once<gemm_tc_kernel<BN, MT, EPI>>((int)C::SMEM);
+  dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + 128 * MT - 1) / (128 * MT)));
+  kern<<<grid, kGemmThreads, C::SMEM, stream>>>(ta, tb, M, N, (int)K, p);
+  return check_launch("gemm_tc_kernel");
+}
+
+template <int EPI>
+static int gemm_dispatch(const void* x, const void* w, int64_t M, int64_t N, int64_t K, const EpiParams& p,
+                         cudaStream_t stream) {
+  if (M <= 128) return launch_gemm<128, 1, EPI>(x, w, M, N, K, p, stream);
+  if (M <= 256) return launch_gemm<128, 2, EPI>(x, w, M, N, K, p, stream);
+  return launch_gemm<256, 2, EPI>(x, w, M, N, K, p, stream);
+}
+
+static int gemm_check(const void* x, const void* w, int64_t M, int64_t N, int64_t K, const char* what) {
+  if (M < 0 || N <= 0 || K <= 0 || K % 64)
+    return set_error(AACC_ERR_INVALID, "%s: need K %% 64 == 0 (M %lld N %lld K %lld)", what, (long long)M,
+                     (long long)N, (long long)K);
+  if (M >= (int64_t(1) << 31) || N >= (int64_t(1) << 31))
+    return set_error(AACC_ERR_UNSUPPORTED, "%s: dimension too large", what);
+  if (!aligned16(x) || !aligned16(w)) return set_error(AACC_ERR_INVALID, "%s: operands must be 16-byte aligned", what);
+  return AACC_OK;
+}
+
+}  // namespace aacc
+
+using namespace aacc;
+
+extern "C" {
+
+int aacc_gemm(const void* x, const void* w, void* out, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+  int st = gemm_check(x, w, M, N, K, "gemm");
+  if (st || M == 0) return st;
+  if (!aligned16(out) || (N % 8)) return set_error(AACC_ERR_INVALID, "gemm: output must be 16-byte aligned rows");
+  EpiParams p{};
+  p.out = (bf16*)out;
+  p.ldo = N;
+  p.err = device_error_ptr();
+  return gemm_dispatch<EPI_STORE>(x, w, M, N, K, p, stream);
+}
+
+int aacc_gemm_silu_mul(const void* x, const void* w_gate_up, void* out, int64_t M, int64_t I, int64_t K,
+                       cudaStream_t stream) {
+  int st = gemm_check(x, w_gate_up, M, 2 * I, K, "gemm_silu_mul");
+  if (st || M == 0) return st;
+  if (I % 64) return set_error(AACC_ERR_INVALID, "gemm_silu_mul: intermediate size must be a multiple of 64");
+  if (!aligned16(out)) return set_error(AACC_ERR_INVALID, "gemm_silu_mul: output must be 16-byte aligned");
+  EpiParams p{};
+  p.out = (bf16*)out;
+  p.ldo = I;
+  p.err = device_error_ptr();
+  return gemm_dispatch<EPI_SILU>(x, w_gate_up, M, 2 * I, K, p, stream);
+}
+
+int aacc_qkv_norm_rope_store(const void* x, const void* w_qkv, const void* q_norm_w, const void* k_norm_w, float eps,
+                             const int64_t* positions, const void* rope_cos_sin, int64_t max_pos,
+                             const int64_t* slot_mapping, void* q_out, void* k_cache, void* v_cache,
+                             int64_t num_blocks, int num_q_heads, int num_kv_heads, int block_size, int64_t M,
+                             int64_t K, cudaStream_t stream) {
+  const int64_t N = (int64_t)(num_q_heads + 2 * num_kv_heads) * 128;
+  int st = gemm_check(x, w_qkv, M, N, K, "qkv_norm_rope_store");
+  if (st || M == 0) return st;
+  if (num_q_heads <= 0 || num_kv_heads <= 0 || block_size <= 0 || num_blocks <= 0 || max_pos <= 0)
+    return set_error(AACC_ERR_INVALID, "qkv_norm_rope_store: bad sizes");
+  if (!aligned16(q_out) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(rope_cos_sin) ||
+      !aligned16(q_norm_w) || !aligned16(k_norm_w))
+    return set_error(AACC_ERR_INVALID, "qkv_norm_rope_store: pointers must be 16-byte aligned");
+  EpiParams p{};
+  p.out = (bf16*)q_out;
+  p.ldo = (int64_t)num_q_heads * 128;
+  p.qn_w = (const bf16*)q_norm_w;
+  p.kn_w = (const bf16*)k_norm_w;
+  p.eps = eps;
+  p.positions = positions;
+  p.rope = (const bf16*)rope_cos_sin;
+  p.max_pos = max_pos;
+  p.slot_mapping = slot_mapping;
+  p.k_cache = (bf16*)k_cache;
+  p.v_cache = (bf16*)v_cache;
+  p.num_slots = num_blocks * block_size;
+  p.Hq = num_q_heads;
+  p.Hkv = num_kv_heads;
+  p.bs = block_size;
+  p.err = device_error_ptr();
+  return gemm_dispatch<EPI_QKV>(x, w_qkv, M, N, K, p, stream);
+}
+
+int64_t aacc_lm_head_workspace_bytes(int64_t M, int64_t vocab) {
+  return M * ((vocab + 127) / 128) * (int64_t)(sizeof(float) + sizeof(int32_t));
+}
+
+int aacc_lm_head_argmax(const void* x, const void* w, int64_t M, int64_t vocab, int64_t K, int64_t vocab_offset,
+                        int64_t* tokens, float* best_val, void* logits, void* workspace, int64_t workspace_bytes,
+                        cudaStream_t stream) {
+  int st = gemm_check(x, w, M, vocab, K, "lm_head_argmax");
+  if (st || M == 0) return st;
+  const int64_t groups = (vocab + 127) / 128;
+  if (!workspace || workspace_bytes < aacc_lm_head_workspace_bytes(M, vocab))
+    return set_error(AACC_ERR_INVALID, "lm_head_argmax: workspace too small");
+  if (logits && (!aligned16(logits) || vocab % 8))
+    return set_error(AACC_ERR_INVALID, "lm_head_argmax: logits rows must be 16-byte aligned");
+  EpiParams p{};
+  p.out = (bf16*)logits;
+  p.ldo = vocab;
+  p.part_val = (float*)workspace;
+  p.part_idx = (int32_t*)((float*)workspace + M * groups);
+  p.n_groups = groups;
+  p.err = device_error_ptr();
+  st = gemm_dispatch<EPI_ARGMAX>(x, w, M, vocab, K, p, stream);
+  if (st) return st;
+  argmax_merge_groups_kernel<<<(unsigned)M, 256, 0, stream>>>(p.part_val, p.part_idx, groups, vocab_offset, tokens,
+                                                              best_val);
+  return check_launch("argmax_merge_groups");
+}
+
+}  // extern "C"

@@ -1,0 +1,76 @@
+// Greedy sampling over materialised logits and the vocab-parallel argmax merge.
+#include "common.cuh"
+#include "host.h"
+
+namespace aacc {
+
+__device__ __forceinline__ void better(float& bv, int64_t& bi, float v, int64_t i) {
+  if (v > bv || (v == bv && i < bi)) {
+    bv = v;
+    bi = i;
+  }
+}
+
+__device__ __forceinline__ void block_argmax(float& bv, int64_t& bi) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float v = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int64_t i = __shfl_xor_sync(0xffffffffu, bi, o);
+    better(bv, bi, v, i);
+  }
+  __shared__ float sv[32];
+  __shared__ int64_t si[32];
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    sv[w] = bv;
+    si[w] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int k = 1; k < (int)(blockDim.x >> 5); ++k) better(bv, bi, sv[k], si[k]);
+}
+
+// torch.argmax semantics on bf16 rows: highest value, first index on ties.
+__global__ void argmax_rows_kernel(const bf16* __restrict__ logits, int64_t vocab, int64_t* __restrict__ tokens) {
+  const int64_t m = blockIdx.x;
+  float bv = -INFINITY;
+  int64_t bi = INT64_MAX;
+  const bf16* row = logits + m * vocab;
+  for (int64_t n = threadIdx.x; n < vocab; n += blockDim.x) better(bv, bi, bf(row[n]), n);
+  block_argmax(bv, bi);
+  if (threadIdx.x == 0) tokens[m] = bi == INT64_MAX ? 0 : bi;
+}
+
+__global__ void argmax_merge_kernel(const float* __restrict__ cv, const int64_t* __restrict__ ci, int shards,
+                                    int64_t* __restrict__ tokens) {
+  const int64_t m = blockIdx.x;
+  float bv = -INFINITY;
+  int64_t bi = INT64_MAX;
+  const int64_t M = gridDim.x;
+  for (int s = threadIdx.x; s < shards; s += blockDim.x) better(bv, bi, cv[s * M + m], ci[s * M + m]);
+  block_argmax(bv, bi);
+  if (threadIdx.x == 0) tokens[m] = bi == INT64_MAX ? 0 : bi;
+}
+
+}  // namespace aacc
+
+using namespace aacc;
+
+extern "C" {
+
+int aacc_argmax_rows(const void* logits, int64_t M, int64_t vocab, int64_t* tokens, cudaStream_t stream) {
+  if (M < 0 || vocab <= 0) return set_error(AACC_ERR_INVALID, "argmax_rows: bad sizes");
+  if (M == 0) return AACC_OK;
+  argmax_rows_kernel<<<(unsigned)M, 512, 0, stream>>>((const bf16*)logits, vocab, tokens);
+  return check_launch("argmax_rows");
+}
+
+int aacc_argmax_merge(const float* cand_val, const int64_t* cand_idx, int64_t M, int shards, int64_t* tokens,
+                      cudaStream_t stream) {
+  if (M < 0 || shards <= 0) return set_error(AACC_ERR_INVALID, "argmax_merge: bad sizes");
+  if (M == 0) return AACC_OK;
+  argmax_merge_kernel<<<(unsigned)M, 32, 0, stream>>>(cand_val, cand_idx, shards, tokens);
+  return check_launch("argmax_merge");
+}
+
+}  // extern "C"

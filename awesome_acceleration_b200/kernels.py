@@ -1,0 +1,187 @@
+"""Tensor-level wrappers over the C ABI (one call = one or two kernel launches).
+
+Tensors must be CUDA, contiguous and of the documented dtype; every call
+launches on the current PyTorch stream, so it composes with CUDA-graph
+capture.  Outputs are allocated here only when the caller passes none.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+BF16 = torch.bfloat16
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _lib_():
+    return _lib.load()
+
+
+def _req(t: torch.Tensor, dtype, name: str):
+    if not t.is_cuda or t.dtype != dtype or not t.is_contiguous():
+        raise ValueError(f"{name}: expected a contiguous CUDA {dtype} tensor, got {t.dtype} "
+                         f"{'cuda' if t.is_cuda else 'cpu'} contiguous={t.is_contiguous()}")
+
+
+# ---------------------------------------------------------------- KV cache
+def kv_store(k: torch.Tensor, v: torch.Tensor, slot_mapping: torch.Tensor, k_cache: torch.Tensor,
+             v_cache: torch.Tensor) -> None:
+    """k/v [T, Hkv, 128] (row-strided views allowed); caches [blocks, Hkv, bs, 128]."""
+    nb, hkv, bs, _ = k_cache.shape
+    _req(slot_mapping, torch.int64, "slot_mapping")
+    _lib.check(_lib_().aacc_kv_store(_p(k), _p(v), k.shape[0], k.stride(0), v.stride(0), _p(slot_mapping),
+                                     _p(k_cache), _p(v_cache), nb, hkv, bs, _stream()), "kv_store")
+
+
+def decode_slot_mapping(rows, seqlens, block_tables, block_size: int, num_blocks: int, out) -> None:
+    _lib.check(_lib_().aacc_decode_slot_mapping(_p(rows), _p(seqlens), _p(block_tables), block_tables.shape[1],
+                                                block_size, num_blocks, _p(out), rows.shape[0], _stream()),
+               "decode_slot_mapping")
+
+
+def advance_seqlens(rows, seqlens, positions=None) -> None:
+    _lib.check(_lib_().aacc_advance_seqlens(_p(rows), _p(seqlens), _p(positions), rows.shape[0], _stream()),
+               "advance_seqlens")
+
+
+def gather_rows(src: torch.Tensor, idx: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty((idx.shape[0],) + tuple(src.shape[1:]), dtype=src.dtype, device=src.device)
+    row_bytes = src[0].numel() * src.element_size()
+    _lib.check(_lib_().aacc_gather_rows(_p(src), src.shape[0], row_bytes, _p(idx), idx.shape[0], _p(out),
+                                        _stream()), "gather_rows")
+    return out
+
+
+# ---------------------------------------------------------------- attention
+def decode_workspace_bytes(batch: int, num_q_heads: int, max_context: int, split_tokens: int = 0) -> int:
+    return int(_lib_().aacc_paged_decode_workspace_bytes(batch, num_q_heads, max_context, split_tokens))
+
+
+def paged_decode_attention(q, k_cache, v_cache, block_tables, rows, seqlens, *, ctx_add: int, scale: float,
+                           max_context: int, workspace: torch.Tensor | None, out=None,
+                           split_tokens: int = 0) -> torch.Tensor:
+    """q [B, Hq, 128] -> out [B, Hq, 128] over seqlens[rows[b]] + ctx_add cached tokens."""
+    B, hq, _ = q.shape
+    nb, hkv, bs, _ = k_cache.shape
+    if out is None:
+        out = torch.empty_like(q)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    _lib.check(_lib_().aacc_paged_decode_attention(
+        _p(q), _p(out), _p(k_cache), _p(v_cache), nb, _p(block_tables), block_tables.shape[1], _p(rows),
+        _p(seqlens), ctx_add, B, hq, hkv, bs, scale, split_tokens, max_context, _p(workspace), ws_bytes,
+        _stream()), "paged_decode_attention")
+    return out
+
+
+def prefill_attention(q, k_cache, v_cache, block_tables, seq_rows, cu_q, ctx_start, *, max_q_len: int,
+                      scale: float, out=None) -> torch.Tensor:
+    """q [T, Hq, 128] packed by cu_q -> out [T, Hq, 128] (causal over cached context + chunk)."""
+    T, hq, _ = q.shape
+    nb, hkv, bs, _ = k_cache.shape
+    if out is None:
+        out = torch.empty_like(q)
+    _lib.check(_lib_().aacc_prefill_attention(
+        _p(q), _p(out), _p(k_cache), _p(v_cache), nb, _p(block_tables), block_tables.shape[1], _p(seq_rows),
+        _p(cu_q), _p(ctx_start), seq_rows.shape[0], max_q_len, hq, hkv, bs, scale, _stream()),
+        "prefill_attention")
+    return out
+
+
+# ---------------------------------------------------------------- norms
+def rmsnorm(x, w, eps: float, out=None):
+    H = x.shape[-1]
+    rows = x.numel() // H
+    if out is None:
+        out = torch.empty_like(x)
+    _lib.check(_lib_().aacc_rmsnorm(_p(x), _p(w), _p(out), rows, H, eps, _stream()), "rmsnorm")
+    return out
+
+
+def add_rmsnorm(delta, residual, w, eps: float, out=None):
+    """residual <- bf16(residual + delta); returns rmsnorm(residual)."""
+    H = residual.shape[-1]
+    rows = residual.numel() // H
+    if out is None:
+        out = torch.empty_like(residual)
+    _lib.check(_lib_().aacc_add_rmsnorm(_p(delta), _p(residual), _p(w), _p(out), rows, H, eps, _stream()),
+               "add_rmsnorm")
+    return out
+
+
+def embed_rmsnorm(ids, table, w, eps: float, residual_out, out):
+    rows = ids.numel()
+    V, H = table.shape
+    _lib.check(_lib_().aacc_embed_rmsnorm(_p(ids), _p(table), V, _p(residual_out), _p(w), _p(out), rows, H, eps,
+                                          _stream()), "embed_rmsnorm")
+    return out
+
+
+# ---------------------------------------------------------------- GEMMs
+def gemm(x, w, out=None):
+    M, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=BF16, device=x.device)
+    _lib.check(_lib_().aacc_gemm(_p(x), _p(w), _p(out), M, N, K, _stream()), "gemm")
+    return out
+
+
+def gemm_silu_mul(x, w_gate_up, out=None):
+    M, K = x.shape
+    I = w_gate_up.shape[0] // 2
+    if out is None:
+        out = torch.empty((M, I), dtype=BF16, device=x.device)
+    _lib.check(_lib_().aacc_gemm_silu_mul(_p(x), _p(w_gate_up), _p(out), M, I, K, _stream()), "gemm_silu_mul")
+    return out
+
+
+def qkv_norm_rope_store(x, w_qkv, q_norm_w, k_norm_w, eps: float, positions, rope_cos_sin, slot_mapping,
+                        k_cache, v_cache, num_q_heads: int, q_out=None):
+    M, K = x.shape
+    nb, hkv, bs, _ = k_cache.shape
+    if q_out is None:
+        q_out = torch.empty((M, num_q_heads, 128), dtype=BF16, device=x.device)
+    _lib.check(_lib_().aacc_qkv_norm_rope_store(
+        _p(x), _p(w_qkv), _p(q_norm_w), _p(k_norm_w), eps, _p(positions), _p(rope_cos_sin), rope_cos_sin.shape[0],
+        _p(slot_mapping), _p(q_out), _p(k_cache), _p(v_cache), nb, num_q_heads, hkv, bs, M, K, _stream()),
+        "qkv_norm_rope_store")
+    return q_out
+
+
+def lm_head_workspace_bytes(M: int, vocab: int) -> int:
+    return int(_lib_().aacc_lm_head_workspace_bytes(M, vocab))
+
+
+def lm_head_argmax(x, w, tokens, workspace, *, logits=None, best_val=None, vocab_offset: int = 0):
+    M, K = x.shape
+    V = w.shape[0]
+    _lib.check(_lib_().aacc_lm_head_argmax(
+        _p(x), _p(w), M, V, K, vocab_offset, _p(tokens), _p(best_val), _p(logits), _p(workspace),
+        workspace.numel() * workspace.element_size(), _stream()), "lm_head_argmax")
+    return tokens
+
+
+def argmax_rows(logits, tokens=None):
+    M, V = logits.shape
+    if tokens is None:
+        tokens = torch.empty(M, dtype=torch.int64, device=logits.device)
+    _lib.check(_lib_().aacc_argmax_rows(_p(logits), M, V, _p(tokens), _stream()), "argmax_rows")
+    return tokens
+
+
+def argmax_merge(cand_val, cand_idx, tokens=None):
+    """cand_val/cand_idx [shards, M] -> tokens [M]."""
+    S, M = cand_val.shape
+    if tokens is None:
+        tokens = torch.empty(M, dtype=torch.int64, device=cand_val.device)
+    _lib.check(_lib_().aacc_argmax_merge(_p(cand_val), _p(cand_idx), M, S, _p(tokens), _stream()), "argmax_merge")
+    return tokens

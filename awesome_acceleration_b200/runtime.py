@@ -1,0 +1,361 @@
+"""Per-step Qwen3 hot path on the B200 kernels (prefill + decode).
+
+``Qwen3Runtime`` owns the flat per-layer weight list, the paged KV cache and
+the static decode buffers, and drives the C-ABI kernels layer by layer:
+
+  decode step (one token per row, all on device, CUDA-graph captured per
+  batch size):
+    slot_mapping <- block_tables/seqlens                  (decode_slot_mapping)
+    res, x       <- embed[ids], rmsnorm                   (embed_rmsnorm)
+    per layer:
+      q, K/V->cache <- x @ Wqkv^T, q/k-norm, RoPE          (qkv_norm_rope_store)
+      o            <- paged attention over seqlens+1       (paged_decode_attention)
+      d            <- o @ Wo^T            [TP: all-reduce]  (gemm)
+      res, x       <- res + d, rmsnorm                     (add_rmsnorm)
+      a            <- silu(x Wg^T) * (x Wu^T)              (gemm_silu_mul)
+      d            <- a @ Wd^T            [TP: all-reduce]  (gemm)
+      res, x       <- res + d, next rmsnorm                (add_rmsnorm)
+    ids          <- argmax(x @ lm_head^T) [TP: vocab shards + merge]
+    seqlens, positions += 1                                (advance_seqlens)
+
+  prefill (packed, chunked): the same layer chain over the chunk's tokens,
+  with K/V stored by the QKV epilogue and causal attention over the paged
+  cache (prefill_attention), then argmax of the last token of every sequence
+  that ends in the chunk.
+
+This is the reference's ``LLM._prefill`` (llm.py:116-208),
+``TransformerBlock.forward`` (model/model.py:202-267) and the TP twins
+(llm_tp.py:397-517, model/model_tp.py:177-324) restructured around fused
+kernels.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import kernels as K
+from .kv_cache import PagedKVCache
+
+
+@dataclass
+class LayerWeights:
+    in_ln: torch.Tensor       # [H]
+    wqkv: torch.Tensor        # [(Hq + 2 Hkv) * 128, H]  (this rank's heads)
+    q_norm: torch.Tensor      # [128]
+    k_norm: torch.Tensor      # [128]
+    wo: torch.Tensor          # [H, Hq * 128]
+    post_ln: torch.Tensor     # [H]
+    w_gate_up: torch.Tensor   # [2 I, H] gate/up interleaved by 64 rows
+    wd: torch.Tensor          # [H, I]
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, group: int = 64) -> torch.Tensor:
+    """Rows [128j, 128j+64) = gate rows [64j, 64j+64), next 64 = up rows."""
+    I, H = gate.shape
+    if I % group:
+        raise ValueError(f"intermediate size {I} must be a multiple of {group}")
+    return torch.stack([gate.view(I // group, group, H), up.view(I // group, group, H)], 1).reshape(2 * I, H)
+
+
+def rope_table(max_pos: int, head_dim: int, theta: float, device, dtype=torch.bfloat16) -> torch.Tensor:
+    """[max_pos][head_dim] = cos[:half] | sin[:half] of the reference's cached
+    RoPE table (model/model.py:63, :72-78), built with the same torch ops.
+
+    The reference converts its whole module, the ``inv_freq`` buffer
+    included, to the model dtype (``cls(config).to(dtype)``,
+    model/model.py:358), so in a bf16 model the positions
+    (``arange(seq_len, dtype=inv_freq.dtype)``) and frequencies are bf16 and
+    every op rounds to bf16.  Reproducing that keeps K/V bit-exact with it."""
+    inv_freq = (1.0 / (theta ** (torch.arange(0, head_dim, 2).float() / head_dim))).to(dtype).to(device)
+    t = torch.arange(max_pos, device=device, dtype=inv_freq.dtype)
+    freqs = torch.outer(t, inv_freq)
+    emb = torch.cat((freqs, freqs), dim=-1)
+    half = head_dim // 2
+    return torch.cat([emb.cos().to(dtype)[:, :half], emb.sin().to(dtype)[:, :half]], dim=-1).contiguous()
+
+
+class TPComm:
+    """Collective hooks of the tensor-parallel path (identity at TP=1)."""
+
+    def __init__(self, rank: int = 0, size: int = 1, group=None):
+        self.rank, self.size, self.group = rank, size, group
+
+    def all_reduce(self, t: torch.Tensor) -> None:
+        if self.size > 1:
+            torch.distributed.all_reduce(t, group=self.group)
+
+    def all_gather(self, out: torch.Tensor, t: torch.Tensor) -> None:
+        torch.distributed.all_gather_into_tensor(out, t, group=self.group)
+
+
+class _DecodeBuffers:
+    def __init__(self, B: int, H: int, Hq: int, I: int, vocab: int, tp: int, max_context: int, device):
+        i64 = dict(dtype=torch.int64, device=device)
+        bf = dict(dtype=torch.bfloat16, device=device)
+        self.meta = torch.zeros((3, B), **i64)  # ids | positions | rows
+        self.ids, self.pos, self.rows = self.meta[0], self.meta[1], self.meta[2]
+        self.slot_map = torch.zeros(B, **i64)
+        self.res = torch.zeros((B, H), **bf)
+        self.x = torch.zeros((B, H), **bf)
+        self.delta = torch.zeros((B, H), **bf)
+        self.q = torch.zeros((B, Hq, 128), **bf)
+        self.attn = torch.zeros((B, Hq, 128), **bf)
+        self.act = torch.zeros((B, I), **bf)
+        ws = K.decode_workspace_bytes(B, Hq, max_context)
+        self.attn_ws = torch.empty(max(ws, 16), dtype=torch.uint8, device=device)
+        self.lm_ws = torch.empty(K.lm_head_workspace_bytes(B, vocab), dtype=torch.uint8, device=device)
+        self.best = torch.zeros(B, dtype=torch.float32, device=device)
+        self.tok = torch.zeros(B, **i64)
+        if tp > 1:
+            self.g_best = torch.zeros((tp, B), dtype=torch.float32, device=device)
+            self.g_tok = torch.zeros((tp, B), **i64)
+
+
+class Qwen3Runtime:
+    def __init__(self, *, hidden: int, intermediate: int, num_q_heads: int, num_kv_heads: int, vocab: int,
+                 eps: float, layers: list[LayerWeights], embed: torch.Tensor, final_norm: torch.Tensor,
+                 lm_head: torch.Tensor, kv: PagedKVCache, rope: torch.Tensor, comm: TPComm | None = None,
+                 vocab_offset: int = 0, max_batch: int = 256, use_graphs: bool = True,
+                 prefill_chunk_tokens: int = 32768):
+        self.comm = comm or TPComm()
+        tp = self.comm.size
+        self.H, self.eps = hidden, eps
+        self.Hq, self.Hkv = num_q_heads // tp, num_kv_heads // tp   # this rank's heads
+        self.I = intermediate // tp
+        self.vocab = vocab                                          # full vocabulary
+        self.vocab_local = lm_head.shape[0]
+        self.vocab_offset = vocab_offset
+        self.layers, self.embed, self.final_norm, self.lm_head = layers, embed, final_norm, lm_head
+        self.kv, self.rope = kv, rope
+        self.scale = 128 ** -0.5
+        self.max_batch = max_batch
+        self.use_graphs = use_graphs
+        self.chunk = prefill_chunk_tokens
+        self.device = embed.device
+        self.max_context = kv.max_blocks * kv.block_size
+        self.buf = _DecodeBuffers(max_batch, hidden, self.Hq, self.I, self.vocab_local, tp, self.max_context,
+                                  self.device)
+        self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self._pinned = torch.zeros((3, max_batch), dtype=torch.int64).pin_memory()
+        self._tok_host = torch.zeros(max_batch, dtype=torch.int64).pin_memory()
+
+    # ------------------------------------------------------------------ layers
+    def _layer_chain(self, x, res, delta, q, attn, act, attend, positions, slot_map):
+        """All layers for rows already embedded into (res, x); `attend(i, q, out)`
+        runs this layer's attention."""
+        L = len(self.layers)
+        kv = self.kv
+        for i, lw in enumerate(self.layers):
+            K.qkv_norm_rope_store(x, lw.wqkv, lw.q_norm, lw.k_norm, self.eps, positions, self.rope, slot_map,
+                                  kv.k[i], kv.v[i], self.Hq, q_out=q)
+            attend(i, q, attn)
+            K.gemm(attn.view(attn.shape[0], -1), lw.wo, out=delta)
+            self.comm.all_reduce(delta)
+            K.add_rmsnorm(delta, res, lw.post_ln, self.eps, out=x)
+            K.gemm_silu_mul(x, lw.w_gate_up, out=act)
+            K.gemm(act, lw.wd, out=delta)
+            self.comm.all_reduce(delta)
+            nxt = self.layers[i + 1].in_ln if i + 1 < L else self.final_norm
+            K.add_rmsnorm(delta, res, nxt, self.eps, out=x)
+
+    def _argmax(self, x, tokens, best, ws, logits=None, g_best=None, g_tok=None):
+        """Greedy token of each row of x; under TP every rank scores its vocab
+        shard and the (value, id) candidates are all-gathered and merged."""
+        K.lm_head_argmax(x, self.lm_head, tokens, ws, logits=logits, best_val=best, vocab_offset=self.vocab_offset)
+        if self.comm.size > 1:
+            self.comm.all_gather(g_best, best)
+            self.comm.all_gather(g_tok, tokens)
+            K.argmax_merge(g_best, g_tok, tokens)
+
+    # ------------------------------------------------------------------ decode
+    def _decode_body(self, B: int, logits=None):
+        b = self.buf
+        kv = self.kv
+        rows, ids, pos = b.rows[:B], b.ids[:B], b.pos[:B]
+        K.decode_slot_mapping(rows, kv.seqlens, kv.block_tables, kv.block_size, kv.num_blocks, b.slot_map[:B])
+        K.embed_rmsnorm(ids, self.embed, self.layers[0].in_ln, self.eps, b.res[:B], b.x[:B])
+
+        def attend(i, q, out):
+            K.paged_decode_attention(q, kv.k[i], kv.v[i], kv.block_tables, rows, kv.seqlens, ctx_add=1,
+                                     scale=self.scale, max_context=self.max_context, workspace=b.attn_ws, out=out)
+
+        self._layer_chain(b.x[:B], b.res[:B], b.delta[:B], b.q[:B], b.attn[:B], b.act[:B], attend, pos,
+                          b.slot_map[:B])
+        g_best = b.g_best[:, :B] if self.comm.size > 1 else None
+        g_tok = b.g_tok[:, :B] if self.comm.size > 1 else None
+        self._argmax(b.x[:B], ids, b.best[:B], b.lm_ws, logits=logits, g_best=g_best, g_tok=g_tok)
+        K.advance_seqlens(rows, kv.seqlens, pos)
+
+    def load_decode_inputs(self, ids, positions, rows) -> None:
+        """Stage one decode batch (host sequences of ints) into the static buffers."""
+        B = len(rows)
+        if B > self.max_batch:
+            raise ValueError(f"decode batch {B} exceeds max_batch {self.max_batch}")
+        p = self._pinned
+        p[0, :B] = torch.as_tensor(ids, dtype=torch.int64)
+        p[1, :B] = torch.as_tensor(positions, dtype=torch.int64)
+        p[2, :B] = torch.as_tensor(rows, dtype=torch.int64)
+        self.buf.meta[:, :B].copy_(p[:, :B], non_blocking=True)
+
+    def reserve_decode(self, rows) -> None:
+        """Host block bookkeeping for one decode step of `rows` (new token at lengths[row])."""
+        kv = self.kv
+        for r in rows:
+            kv.reserve(r, int(kv.lengths[r]) + 1)
+        kv.sync()
+
+    def decode_step(self, rows, logits: torch.Tensor | None = None) -> torch.Tensor:
+        """Run one decode step on the staged inputs of `rows` (host list).  The
+        next tokens overwrite buf.ids[:B] (device); positions/seqlens advance."""
+        B = len(rows)
+        self.reserve_decode(rows)
+        if logits is not None or not self.use_graphs:
+            self._decode_body(B, logits)
+        else:
+            g = self._graphs.get(B)
+            if g is None:
+                g = self._capture(B)
+            g.replay()
+        for r in rows:
+            self.kv.lengths[r] += 1
+        return self.buf.ids[:B]
+
+    def _capture(self, B: int) -> torch.cuda.CUDAGraph:
+        # Capturing must not change state: run the body once eagerly on a
+        # side stream (warms every kernel), undo its seqlen/position advance,
+        # then capture.
+        b, kv = self.buf, self.kv
+        saved_meta = b.meta[:, :B].clone()
+        saved_len = kv.seqlens.clone()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self._decode_body(B)
+        torch.cuda.current_stream().wait_stream(s)
+        b.meta[:, :B].copy_(saved_meta)
+        kv.seqlens.copy_(saved_len)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._decode_body(B)
+        b.meta[:, :B].copy_(saved_meta)
+        kv.seqlens.copy_(saved_len)
+        self._graphs[B] = g
+        return g
+
+    def read_tokens(self, B: int) -> list[int]:
+        """D2H of the last decode step's tokens (synchronises the stream)."""
+        t = self._tok_host[:B]
+        t.copy_(self.buf.ids[:B], non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return t.tolist()
+
+    # ------------------------------------------------------------------ prefill
+    def prefill(self, sequences: list[list[int]], rows: list[int], *, positions: list[list[int]] | None = None,
+                store_lengths: list[int] | None = None, all_logits: bool = False, last_logits: bool = False):
+        """Packed (chunked) prefill of whole prompts into `rows`.
+
+        Returns the greedy next token of every sequence (device int64 [n]);
+        with ``last_logits`` also the bf16 logits of the last tokens [n, V];
+        with ``all_logits`` the logits of every token [T, V] instead."""
+        kv = self.kv
+        n = len(sequences)
+        lens = [len(s) for s in sequences]
+        if min(lens) <= 0:
+            raise ValueError("empty prompt")
+        for r, L in zip(rows, lens):
+            kv.reserve(r, L)
+        kv.sync()
+        T = sum(lens)
+        dev = self.device
+        flat = np.fromiter((t for s in sequences for t in s), dtype=np.int64, count=T)
+        if positions is None:
+            pos = np.concatenate([np.arange(L, dtype=np.int64) for L in lens])
+        else:
+            pos = np.concatenate([np.asarray(p, dtype=np.int64) for p in positions])
+        smap = np.concatenate([kv.slot_mapping(r, 0, L) for r, L in zip(rows, lens)])
+        host = torch.from_numpy(np.stack([flat, pos, smap])).pin_memory()
+        meta = host.to(dev, non_blocking=True)
+        ids_d, pos_d, smap_d = meta[0], meta[1], meta[2]
+        tokens = torch.empty(n, dtype=torch.int64, device=dev)
+        V = self.vocab if self.comm.size == 1 else self.vocab_local
+        out_logits = None
+        if all_logits:
+            out_logits = torch.empty((T, V), dtype=torch.bfloat16, device=dev)
+        elif last_logits:
+            out_logits = torch.empty((n, V), dtype=torch.bfloat16, device=dev)
+
+        # Chunk plan: pieces (seq index, start, end) with at most self.chunk tokens per chunk.
+        chunks, cur, cur_tok = [], [], 0
+        offs = np.concatenate([[0], np.cumsum(lens)])
+        for si, L in enumerate(lens):
+            st = 0
+            while st < L:
+                take = min(L - st, self.chunk - cur_tok)
+                cur.append((si, st, st + take))
+                cur_tok += take
+                st += take
+                if cur_tok == self.chunk:
+                    chunks.append(cur)
+                    cur, cur_tok = [], 0
+        if cur:
+            chunks.append(cur)
+
+        H = self.H
+        maxT = max(sum(e - s for _, s, e in ch) for ch in chunks)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        res = torch.empty((maxT, H), **bf)
+        x = torch.empty((maxT, H), **bf)
+        delta = torch.empty((maxT, H), **bf)
+        q = torch.empty((maxT, self.Hq, 128), **bf)
+        attn = torch.empty((maxT, self.Hq, 128), **bf)
+        act = torch.empty((maxT, self.I), **bf)
+        lm_ws = torch.empty(K.lm_head_workspace_bytes(maxT if all_logits else n, self.vocab_local),
+                            dtype=torch.uint8, device=dev)
+        best = torch.empty(maxT if all_logits else n, dtype=torch.float32, device=dev)
+        for ch in chunks:
+            t0 = int(offs[ch[0][0]] + ch[0][1])
+            Tc = sum(e - s for _, s, e in ch)
+            npc = len(ch)
+            # Sequences whose last token lies in this chunk: consecutive indices [a, a + m).
+            ends = [(si, int(offs[si] + e - 1 - t0)) for si, s, e in ch if e == lens[si]]
+            # Per-piece attention metadata: block-table row, query offsets, context before the piece.
+            cu = np.zeros(npc + 1, dtype=np.int64)
+            cu[1:] = np.cumsum([e - s for _, s, e in ch])
+            m64 = np.concatenate([np.asarray([rows[si] for si, _, _ in ch], dtype=np.int64),
+                                  np.asarray([r for _, r in ends], dtype=np.int64)])
+            m32 = np.concatenate([cu, np.asarray([s for _, s, _ in ch], dtype=np.int64)]).astype(np.int32)
+            d64 = torch.from_numpy(m64).pin_memory().to(dev, non_blocking=True)
+            d32 = torch.from_numpy(m32).pin_memory().to(dev, non_blocking=True)
+            seq_rows, last_idx = d64[:npc], d64[npc:]
+            cu_q, ctx0 = d32[:npc + 1], d32[npc + 1:]
+            max_q = max(e - s for _, s, e in ch)
+            xs, rs, ds = x[:Tc], res[:Tc], delta[:Tc]
+            K.embed_rmsnorm(ids_d[t0:t0 + Tc], self.embed, self.layers[0].in_ln, self.eps, rs, xs)
+
+            def attend(i, qq, out, seq_rows=seq_rows, cu_q=cu_q, ctx0=ctx0, max_q=max_q):
+                K.prefill_attention(qq, kv.k[i], kv.v[i], kv.block_tables, seq_rows, cu_q, ctx0, max_q_len=max_q,
+                                    scale=self.scale, out=out)
+
+            self._layer_chain(xs, rs, ds, q[:Tc], attn[:Tc], act[:Tc], attend, pos_d[t0:t0 + Tc],
+                              smap_d[t0:t0 + Tc])
+            if all_logits:
+                tk = torch.empty(Tc, dtype=torch.int64, device=dev)
+                K.lm_head_argmax(xs, self.lm_head, tk, lm_ws, logits=out_logits[t0:t0 + Tc], best_val=best[:Tc],
+                                 vocab_offset=self.vocab_offset)
+            elif ends:
+                a, m = ends[0][0], len(ends)
+                hx = K.gather_rows(xs, last_idx)
+                lg = out_logits[a:a + m] if last_logits else None
+                if self.comm.size > 1:
+                    gb = torch.empty((self.comm.size, m), dtype=torch.float32, device=dev)
+                    gt = torch.empty((self.comm.size, m), dtype=torch.int64, device=dev)
+                    self._argmax(hx, tokens[a:a + m], best[a:a + m], lm_ws, logits=lg, g_best=gb, g_tok=gt)
+                else:
+                    self._argmax(hx, tokens[a:a + m], best[a:a + m], lm_ws, logits=lg)
+        if all_logits:
+            last = torch.from_numpy(offs[1:] - 1).to(dev)
+            K.argmax_rows(K.gather_rows(out_logits, last), tokens)
+        kv.set_lengths(rows, store_lengths if store_lengths is not None else lens)
+        return (tokens, out_logits) if (all_logits or last_logits) else tokens

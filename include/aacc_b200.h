@@ -1,0 +1,187 @@
+/*
+ * aacc_b200.h — C ABI of the B200-native (sm_100a) Qwen3 per-step hot path.
+ *
+ * Every entry point takes raw device pointers, 64-bit sizes and a CUDA
+ * stream; none allocates memory (KV pools, workspaces and outputs are owned
+ * by the caller).  All tensors are contiguous row-major, bf16 unless stated.
+ * Return value: AACC_OK (0) or an AACC_ERR_* code; aacc_last_error() then
+ * describes the failure (thread-local).  Kernels never trap: an out-of-range
+ * block id, cache slot, position or token id, or a device wait that ran out
+ * of iterations, skips the access and ORs a code into the device error word
+ * read by aacc_get_device_error().
+ *
+ * Each declaration cites the reference code it replaces
+ * (yijichar/AWesome_ACceleration, path:line).
+ *
+ * Paged KV cache layout (per layer, K and V separately):
+ *   cache[num_blocks][num_kv_heads][block_size][128]   (bf16)
+ * A sequence owns a row of `block_tables` (int32 [rows][max_blocks]); token
+ * `pos` lives at flat slot block_tables[row][pos / block_size] * block_size
+ * + pos % block_size.  This replaces the reference's slot-contiguous cache
+ * K[num_slots][max_seq_len][Hkv][D] with flat index slot*max_seq_len + pos
+ * (model/model.py:324-336, llm.py:139-140).  block_size must be a multiple
+ * of 64; head_dim is 128 (all Qwen3 models).
+ */
+#ifndef AACC_B200_H
+#define AACC_B200_H
+
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AACC_OK 0
+#define AACC_ERR_INVALID 1     /* bad shape, alignment or argument */
+#define AACC_ERR_CUDA 2        /* a CUDA runtime call or launch failed */
+#define AACC_ERR_UNSUPPORTED 3 /* configuration outside the compiled kernels */
+
+/* ---- library / error plumbing ------------------------------------------ */
+int aacc_version(void);
+const char* aacc_last_error(void);
+/* Copy the device error word of the current device into *out (synchronous). */
+int aacc_get_device_error(unsigned* out);
+int aacc_clear_device_error(void);
+
+/* ---- KV cache ------------------------------------------------------------ */
+
+/* Scatter new K/V rows into the paged cache: row t of k/v (Hkv*128 values,
+ * row strides in elements) goes to flat slot slot_mapping[t]; -1 skips.
+ * Replaces the KV write inside flash_attn_with_kvcache (model/model.py:233-241)
+ * and the prefill index_copy_ scatter (llm.py:171-175; llm_tp.py:454-468). */
+int aacc_kv_store(const void* k, const void* v, int64_t num_tokens, int64_t k_row_stride,
+                  int64_t v_row_stride, const int64_t* slot_mapping, void* k_cache, void* v_cache,
+                  int64_t num_blocks, int num_kv_heads, int block_size, cudaStream_t stream);
+
+/* Flat cache slot of the next token of each decode row:
+ * out[b] = block_tables[row][n / bs] * bs + n % bs, n = seqlens[row],
+ * row = slot_indices[b].  (The position the reference writes at,
+ * cache_seqlens[slot], model/model.py:233-238.) */
+int aacc_decode_slot_mapping(const int64_t* slot_indices, const int32_t* seqlens,
+                             const int32_t* block_tables, int64_t max_blocks, int block_size,
+                             int64_t num_blocks, int64_t* slot_mapping_out, int64_t batch,
+                             cudaStream_t stream);
+
+/* seqlens[slot_indices[b]] += 1 for b < batch
+ * (model/model.py:241 `_cache_seqlens[slot_indices] += 1`); when positions
+ * is not NULL also positions[b] += 1 (the scheduler's `pos += 1`,
+ * llm.py:419), so a decode step can be replayed on device. */
+int aacc_advance_seqlens(const int64_t* slot_indices, int32_t* seqlens, int64_t* positions, int64_t batch,
+                         cudaStream_t stream);
+
+/* dst[i] = src[idx[i]] for i < n, rows of row_bytes bytes (multiple of 16):
+ * the last-token gather of the packed prefill (llm.py:199-201
+ * `hidden[cu_seqlens[1:] - 1]`). */
+int aacc_gather_rows(const void* src, int64_t n_src, int64_t row_bytes, const int64_t* idx, int64_t n, void* dst,
+                     cudaStream_t stream);
+
+/* ---- attention ----------------------------------------------------------- */
+
+/* Workspace bytes aacc_paged_decode_attention needs for `batch` rows with at
+ * most `max_context` tokens each. */
+int64_t aacc_paged_decode_workspace_bytes(int64_t batch, int num_q_heads, int64_t max_context,
+                                          int split_tokens);
+
+/* Decode attention of one query token per row over its paged context of
+ * seqlens[row] + ctx_add tokens (GQA, softmax scale `scale`, non-causal).
+ * q, out: [batch][num_q_heads][128].  split_tokens (multiple of 64, 0 =
+ * default) is the context length one CTA streams; longer contexts are split
+ * and merged.  Replaces flash_attn_with_kvcache (model/model.py:233-240,
+ * model/model_tp.py:204-211). */
+int aacc_paged_decode_attention(const void* q, void* out, const void* k_cache, const void* v_cache,
+                                int64_t num_blocks, const int32_t* block_tables, int64_t max_blocks,
+                                const int64_t* slot_indices, const int32_t* seqlens, int ctx_add,
+                                int64_t batch, int num_q_heads, int num_kv_heads, int block_size,
+                                float scale, int split_tokens, int64_t max_context, void* workspace,
+                                int64_t workspace_bytes, cudaStream_t stream);
+
+/* Causal (chunked) prefill attention over the paged cache.  Sequence s owns
+ * query rows [cu_q[s], cu_q[s+1]) of q/out ([T][num_q_heads][128]) at
+ * positions ctx_start[s] + i; its K/V (earlier chunks and this chunk) are
+ * already in the cache under block-table row seq_rows[s].  max_q_len bounds
+ * cu_q[s+1]-cu_q[s].  Replaces flash_attn_varlen_func (llm.py:178-184,
+ * llm_tp.py:471-477) and flash_attn_func (model/model.py:253-254). */
+int aacc_prefill_attention(const void* q, void* out, const void* k_cache, const void* v_cache,
+                           int64_t num_blocks, const int32_t* block_tables, int64_t max_blocks,
+                           const int64_t* seq_rows, const int32_t* cu_q, const int32_t* ctx_start,
+                           int64_t num_seqs, int64_t max_q_len, int num_q_heads, int num_kv_heads,
+                           int block_size, float scale, cudaStream_t stream);
+
+/* ---- RMSNorm ------------------------------------------------------------- */
+
+/* y = w * bf16(x * rsqrt(mean(x^2) + eps)), rows of `hidden` (multiple of
+ * 1024).  RMSNorm.forward, model/model.py:47-52. */
+int aacc_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t hidden, float eps,
+                 cudaStream_t stream);
+
+/* residual = bf16(residual + delta); y = rmsnorm(residual).  The residual add
+ * and the next pre-norm of TransformerBlock.forward (model/model.py:259-263,
+ * :265 + next layer :213 / final norm :285). */
+int aacc_add_rmsnorm(const void* delta, void* residual, const void* w, void* y, int64_t rows,
+                     int64_t hidden, float eps, cudaStream_t stream);
+
+/* residual = table[ids]; y = rmsnorm(residual).  embed_tokens + first
+ * input_layernorm (model/model.py:280, :213). */
+int aacc_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, void* residual,
+                       const void* w, void* y, int64_t rows, int64_t hidden, float eps,
+                       cudaStream_t stream);
+
+/* ---- GEMMs (tcgen05 / TMEM, TMA-fed) --------------------------------------
+ * x: [M][K] activations, w: [N][K] weights (nn.Linear layout); K multiple
+ * of 64; fp32 accumulation, bf16 outputs. */
+
+/* out[M][N] = x @ w^T.  nn.Linear / F.linear (o_proj model/model.py:258,
+ * down_proj :190, RowParallelLinear parallel_layers.py:190). */
+int aacc_gemm(const void* x, const void* w, void* out, int64_t M, int64_t N, int64_t K,
+              cudaStream_t stream);
+
+/* out[M][I] = bf16(silu(bf16(x@Wg^T))) * bf16(x@Wu^T), rounded per op as the
+ * eager reference.  w_gate_up rows interleave gate/up in groups of 64:
+ * rows [128j, 128j+64) = gate rows [64j, 64j+64), the next 64 = up rows.
+ * MLP.forward, model/model.py:189-190 (MLPTP.forward model/model_tp.py:294-299). */
+int aacc_gemm_silu_mul(const void* x, const void* w_gate_up, void* out, int64_t M, int64_t I,
+                       int64_t K, cudaStream_t stream);
+
+/* Fused QKV projection + per-head q/k RMSNorm + RoPE + KV-cache store.
+ * w_qkv: [(Hq + 2*Hkv) * 128][K] rows [Q | K | V] (Attention.fuse_qkv,
+ * model/model.py:132-154).  q_out: [M][Hq][128].  K/V rows go to
+ * k_cache/v_cache at slot_mapping[m] (-1 skips).  rope_cos_sin:
+ * [max_pos][128] bf16 = cos[64] | sin[64] of the reference's cached table.
+ * Replaces model/model.py:219-226 (+ RotaryEmbedding :80-92) and the KV
+ * writes of :233-250 / llm.py:153-175. */
+int aacc_qkv_norm_rope_store(const void* x, const void* w_qkv, const void* q_norm_w,
+                             const void* k_norm_w, float eps, const int64_t* positions,
+                             const void* rope_cos_sin, int64_t max_pos, const int64_t* slot_mapping,
+                             void* q_out, void* k_cache, void* v_cache, int64_t num_blocks,
+                             int num_q_heads, int num_kv_heads, int block_size, int64_t M,
+                             int64_t K, cudaStream_t stream);
+
+/* Workspace bytes for aacc_lm_head_argmax. */
+int64_t aacc_lm_head_workspace_bytes(int64_t M, int64_t vocab);
+
+/* Greedy next token: tokens[m] = argmax_n bf16(x[m] @ w[n]^T) (first index
+ * on ties) without materialising logits.  Optionally also writes bf16
+ * logits [M][vocab] (logits may be NULL).  vocab_offset is added to the
+ * returned ids (vocab-parallel shards); best_val (may be NULL) receives the
+ * winning logit as fp32.  Tied lm_head + greedy sampling
+ * (model/model.py:316-318, llm.py:215-219). */
+int aacc_lm_head_argmax(const void* x, const void* w, int64_t M, int64_t vocab, int64_t K,
+                        int64_t vocab_offset, int64_t* tokens, float* best_val, void* logits,
+                        void* workspace, int64_t workspace_bytes, cudaStream_t stream);
+
+/* Greedy sample from materialised bf16 logits [M][vocab] (llm.py:218). */
+int aacc_argmax_rows(const void* logits, int64_t M, int64_t vocab, int64_t* tokens,
+                     cudaStream_t stream);
+
+/* Vocab-parallel argmax merge: candidates [shards][M] (value, global id),
+ * as all-gathered from every rank's aacc_lm_head_argmax -> tokens[M];
+ * highest value wins, lowest id on ties (the global argmax the reference's
+ * rank-0 lm_head computes, model/model_tp.py:369-373 + llm_tp.py:612-614). */
+int aacc_argmax_merge(const float* cand_val, const int64_t* cand_idx, int64_t M, int shards,
+                      int64_t* tokens, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AACC_B200_H */
