@@ -21,6 +21,7 @@ F32 = ctypes.c_float
 SIGNATURES: dict[str, tuple] = {
     "aacc_version": (I32, []),
     "aacc_last_error": (ctypes.c_char_p, []),
+    "aacc_launch_count": (ctypes.c_ulonglong, []),
     "aacc_get_device_error": (I32, [P]),
     "aacc_clear_device_error": (I32, []),
     "aacc_kv_store": (I32, [P, P, I64, I64, I64, P, P, P, I64, I32, I32, P]),

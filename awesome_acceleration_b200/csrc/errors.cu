@@ -5,6 +5,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -24,7 +25,10 @@ int set_error(int status, const char* fmt, ...) {
   return status;
 }
 
+static std::atomic<unsigned long long> g_launches{0};
+
 int check_launch(const char* what) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(AACC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   return AACC_OK;
@@ -84,6 +88,8 @@ extern "C" {
 int aacc_version(void) { return 1; }
 
 const char* aacc_last_error(void) { return aacc::t_msg; }
+
+unsigned long long aacc_launch_count(void) { return aacc::g_launches.load(std::memory_order_relaxed); }
 
 int aacc_get_device_error(unsigned* out) {
   if (!out) return aacc::set_error(AACC_ERR_INVALID, "null output");

@@ -363,6 +363,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll 1
   for (int g = 0; g < BN / 128; ++g) {
     if (MT == 1 && (g & 1) != wset) continue;
+    // A 128-column group entirely past N (the tail tile of a BN=256 grid)
+    // has nothing to store and no partial slot; skip it (warp-uniform).
+    if (n_base + g * 128 >= N) continue;
     epilogue_group<EPI>(trow + g * 128, m, row_ok, n_base + g * 128, N, p);
   }
 

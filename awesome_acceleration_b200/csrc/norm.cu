@@ -1,6 +1,7 @@
 // RMSNorm family: plain, fused residual-add + RMSNorm, and fused embedding
-// gather + RMSNorm.  One 128-thread CTA per row; each thread keeps its
-// hidden/1024 x 8 values in registers (16-byte vector loads).
+// gather + RMSNorm.  One CTA per row with min(128, hidden/8) threads; each
+// thread keeps V x 8 values in registers (16-byte vector loads), V =
+// hidden / (8 * threads).
 //
 // Rounding follows the eager reference (model/model.py:47-52): fp32 sum of
 // squares, x * rsqrt(mean + eps) rounded to bf16, then the bf16 weight
@@ -11,25 +12,25 @@
 
 namespace aacc {
 
-constexpr int kNormThreads = 128;
+constexpr int kNormMaxThreads = 128;
 
-template <int V>  // uint4 vectors per thread: hidden = V * 8 * 128
+template <int V>
 __device__ __forceinline__ void norm_row(float (&x)[V * 8], const bf16* __restrict__ w, bf16* __restrict__ y,
                                          float eps, int hidden) {
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < V * 8; ++i) ss += x[i] * x[i];
-  __shared__ float red[kNormThreads / 32];
+  __shared__ float red[kNormMaxThreads / 32];
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
   float tot = 0.f;
-#pragma unroll
-  for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
+  const int nw = blockDim.x >> 5;
+  for (int i = 0; i < nw; ++i) tot += red[i];
   const float r = rsqrtf(tot / (float)hidden + eps);
 #pragma unroll
   for (int v = 0; v < V; ++v) {
-    const int col = (v * kNormThreads + threadIdx.x) * 8;
+    const int col = (v * blockDim.x + threadIdx.x) * 8;
     uint4 wv = *reinterpret_cast<const uint4*>(w + col);
     const uint32_t* wu = reinterpret_cast<const uint32_t*>(&wv);
     uint4 ov;
@@ -48,7 +49,7 @@ template <int V>
 __device__ __forceinline__ void load_row(float (&x)[V * 8], const bf16* __restrict__ src) {
 #pragma unroll
   for (int v = 0; v < V; ++v) {
-    const int col = (v * kNormThreads + threadIdx.x) * 8;
+    const int col = (v * blockDim.x + threadIdx.x) * 8;
     uint4 u = *reinterpret_cast<const uint4*>(src + col);
     const uint32_t* p = reinterpret_cast<const uint32_t*>(&u);
 #pragma unroll
@@ -61,8 +62,9 @@ __device__ __forceinline__ void load_row(float (&x)[V * 8], const bf16* __restri
 }
 
 template <int V>
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
-                                                               bf16* __restrict__ y, int hidden, float eps) {
+__global__ void __launch_bounds__(kNormMaxThreads) rmsnorm_kernel(const bf16* __restrict__ x,
+                                                                  const bf16* __restrict__ w, bf16* __restrict__ y,
+                                                                  int hidden, float eps) {
   const int64_t row = blockIdx.x;
   float v[V * 8];
   load_row<V>(v, x + row * hidden);
@@ -70,7 +72,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const bf16* __res
 }
 
 template <int V>
-__global__ void __launch_bounds__(kNormThreads)
+__global__ void __launch_bounds__(kNormMaxThreads)
     add_rmsnorm_kernel(const bf16* __restrict__ delta, bf16* __restrict__ residual, const bf16* __restrict__ w,
                        bf16* __restrict__ y, int hidden, float eps) {
   const int64_t row = blockIdx.x;
@@ -79,7 +81,7 @@ __global__ void __launch_bounds__(kNormThreads)
   load_row<V>(d, delta + row * hidden);
 #pragma unroll
   for (int vv = 0; vv < V; ++vv) {
-    const int col = (vv * kNormThreads + threadIdx.x) * 8;
+    const int col = (vv * blockDim.x + threadIdx.x) * 8;
     uint4 ov;
     uint32_t* ou = reinterpret_cast<uint32_t*>(&ov);
 #pragma unroll
@@ -95,7 +97,7 @@ __global__ void __launch_bounds__(kNormThreads)
 }
 
 template <int V>
-__global__ void __launch_bounds__(kNormThreads)
+__global__ void __launch_bounds__(kNormMaxThreads)
     embed_rmsnorm_kernel(const int64_t* __restrict__ ids, const bf16* __restrict__ table, int64_t vocab,
                          bf16* __restrict__ residual, const bf16* __restrict__ w, bf16* __restrict__ y, int hidden,
                          float eps, unsigned* err) {
@@ -109,18 +111,21 @@ __global__ void __launch_bounds__(kNormThreads)
   load_row<V>(a, table + id * hidden);
 #pragma unroll
   for (int vv = 0; vv < V; ++vv) {
-    const int col = (vv * kNormThreads + threadIdx.x) * 8;
+    const int col = (vv * blockDim.x + threadIdx.x) * 8;
     *reinterpret_cast<uint4*>(residual + row * hidden + col) =
         *reinterpret_cast<const uint4*>(table + id * hidden + col);
   }
   norm_row<V>(a, w, y + row * hidden, eps, hidden);
 }
 
-static int norm_check(int64_t rows, int64_t hidden, const char* what) {
-  if (rows < 0 || hidden <= 0 || hidden % 1024 || hidden > 8192)
-    return set_error(AACC_ERR_UNSUPPORTED, "%s: hidden %lld must be a multiple of 1024 up to 8192", what,
-                     (long long)hidden);
+// threads = min(128, hidden/8) (a multiple of 32); V = hidden / (8 * threads).
+static int norm_shape(int64_t rows, int64_t hidden, const char* what, int* threads, int* V) {
+  if (rows < 0 || hidden < 256 || hidden % 256 || (hidden > 1024 && hidden % 1024) || hidden > 8192)
+    return set_error(AACC_ERR_UNSUPPORTED, "%s: hidden %lld must be 256..1024 in steps of 256 or a multiple of 1024 "
+                     "up to 8192", what, (long long)hidden);
   if (rows > 0x7fffffff) return set_error(AACC_ERR_INVALID, "%s: too many rows", what);
+  *threads = hidden >= 1024 ? 128 : (int)(hidden / 8);
+  *V = (int)(hidden / (8 * *threads));
   return AACC_OK;
 }
 
@@ -128,22 +133,23 @@ static int norm_check(int64_t rows, int64_t hidden, const char* what) {
 
 using namespace aacc;
 
-#define AACC_NORM_DISPATCH(KERNEL, ...)                                                                  \
-  switch (hidden / 1024) {                                                                               \
-    case 1: KERNEL<1><<<(unsigned)rows, kNormThreads, 0, stream>>>(__VA_ARGS__); break;                   \
-    case 2: KERNEL<2><<<(unsigned)rows, kNormThreads, 0, stream>>>(__VA_ARGS__); break;                   \
-    case 3: KERNEL<3><<<(unsigned)rows, kNormThreads, 0, stream>>>(__VA_ARGS__); break;                   \
-    case 4: KERNEL<4><<<(unsigned)rows, kNormThreads, 0, stream>>>(__VA_ARGS__); break;                   \
-    case 5: KERNEL<5><<<(unsigned)rows, kNormThreads, 0, stream>>>(__VA_ARGS__); break;                   \
-    case 6: KERNEL<6><<<(unsigned)rows, kNormThreads, 0, stream>>>(__VA_ARGS__); break;                   \
-    case 7: KERNEL<7><<<(unsigned)rows, kNormThreads, 0, stream>>>(__VA_ARGS__); break;                   \
-    default: KERNEL<8><<<(unsigned)rows, kNormThreads, 0, stream>>>(__VA_ARGS__); break;                  \
+#define AACC_NORM_DISPATCH(KERNEL, ...)                                                       \
+  switch (V) {                                                                                \
+    case 1: KERNEL<1><<<(unsigned)rows, threads, 0, stream>>>(__VA_ARGS__); break;            \
+    case 2: KERNEL<2><<<(unsigned)rows, threads, 0, stream>>>(__VA_ARGS__); break;            \
+    case 3: KERNEL<3><<<(unsigned)rows, threads, 0, stream>>>(__VA_ARGS__); break;            \
+    case 4: KERNEL<4><<<(unsigned)rows, threads, 0, stream>>>(__VA_ARGS__); break;            \
+    case 5: KERNEL<5><<<(unsigned)rows, threads, 0, stream>>>(__VA_ARGS__); break;            \
+    case 6: KERNEL<6><<<(unsigned)rows, threads, 0, stream>>>(__VA_ARGS__); break;            \
+    case 7: KERNEL<7><<<(unsigned)rows, threads, 0, stream>>>(__VA_ARGS__); break;            \
+    default: KERNEL<8><<<(unsigned)rows, threads, 0, stream>>>(__VA_ARGS__); break;           \
   }
 
 extern "C" {
 
 int aacc_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t hidden, float eps, cudaStream_t stream) {
-  int st = norm_check(rows, hidden, "rmsnorm");
+  int threads, V;
+  int st = norm_shape(rows, hidden, "rmsnorm", &threads, &V);
   if (st || rows == 0) return st;
   AACC_NORM_DISPATCH(rmsnorm_kernel, (const bf16*)x, (const bf16*)w, (bf16*)y, (int)hidden, eps)
   return check_launch("rmsnorm");
@@ -151,7 +157,8 @@ int aacc_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t hi
 
 int aacc_add_rmsnorm(const void* delta, void* residual, const void* w, void* y, int64_t rows, int64_t hidden, float eps,
                      cudaStream_t stream) {
-  int st = norm_check(rows, hidden, "add_rmsnorm");
+  int threads, V;
+  int st = norm_shape(rows, hidden, "add_rmsnorm", &threads, &V);
   if (st || rows == 0) return st;
   AACC_NORM_DISPATCH(add_rmsnorm_kernel, (const bf16*)delta, (bf16*)residual, (const bf16*)w, (bf16*)y, (int)hidden,
                      eps)
@@ -160,7 +167,8 @@ int aacc_add_rmsnorm(const void* delta, void* residual, const void* w, void* y, 
 
 int aacc_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, void* residual, const void* w, void* y,
                        int64_t rows, int64_t hidden, float eps, cudaStream_t stream) {
-  int st = norm_check(rows, hidden, "embed_rmsnorm");
+  int threads, V;
+  int st = norm_shape(rows, hidden, "embed_rmsnorm", &threads, &V);
   if (st || rows == 0) return st;
   unsigned* err = device_error_ptr();
   AACC_NORM_DISPATCH(embed_rmsnorm_kernel, ids, (const bf16*)table, vocab, (bf16*)residual, (const bf16*)w, (bf16*)y,

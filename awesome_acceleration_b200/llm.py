@@ -254,6 +254,7 @@ class LLM:
                 seqs = [r.token_ids[i] for r, i, _ in new_work]
                 slots = [s for _, _, s in new_work]
                 toks = rt.prefill(seqs, slots).tolist()
+                rt.d2h_bytes += 8 * len(toks)
                 self.stats["prefill_s"] += time.perf_counter() - t0
                 self.stats["prefill_tokens"] += sum(len(s) for s in seqs)
                 for (req, idx, slot), tok in zip(new_work, toks):

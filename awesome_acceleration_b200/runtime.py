@@ -35,6 +35,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
+from . import _lib
 from . import kernels as K
 from .kv_cache import PagedKVCache
 
@@ -138,6 +139,10 @@ class Qwen3Runtime:
         self.buf = _DecodeBuffers(max_batch, hidden, self.Hq, self.I, self.vocab_local, tp, self.max_context,
                                   self.device)
         self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.graph_launches: dict[int, int] = {}  # kernels per replay of the batch-B graph
+        self.graph_replays = 0
+        self.h2d_bytes = 0  # host->device bytes staged by this runtime
+        self.d2h_bytes = 0
         self._pinned = torch.zeros((3, max_batch), dtype=torch.int64).pin_memory()
         self._tok_host = torch.zeros(max_batch, dtype=torch.int64).pin_memory()
 
@@ -193,11 +198,25 @@ class Qwen3Runtime:
         B = len(rows)
         if B > self.max_batch:
             raise ValueError(f"decode batch {B} exceeds max_batch {self.max_batch}")
+        # The pinned staging buffer may still feed an in-flight copy.
+        torch.cuda.current_stream().synchronize()
         p = self._pinned
         p[0, :B] = torch.as_tensor(ids, dtype=torch.int64)
         p[1, :B] = torch.as_tensor(positions, dtype=torch.int64)
         p[2, :B] = torch.as_tensor(rows, dtype=torch.int64)
         self.buf.meta[:, :B].copy_(p[:, :B], non_blocking=True)
+        self.h2d_bytes += 3 * B * 8
+
+    def load_positions_rows(self, positions, rows) -> None:
+        """Stage positions and rows only; the ids are already on the device
+        (e.g. the prefill's next tokens copied into buf.ids)."""
+        B = len(rows)
+        torch.cuda.current_stream().synchronize()
+        p = self._pinned
+        p[1, :B] = torch.as_tensor(positions, dtype=torch.int64)
+        p[2, :B] = torch.as_tensor(rows, dtype=torch.int64)
+        self.buf.meta[1:, :B].copy_(p[1:, :B], non_blocking=True)
+        self.h2d_bytes += 2 * B * 8
 
     def reserve_decode(self, rows) -> None:
         """Host block bookkeeping for one decode step of `rows` (new token at lengths[row])."""
@@ -218,6 +237,7 @@ class Qwen3Runtime:
             if g is None:
                 g = self._capture(B)
             g.replay()
+            self.graph_replays += 1
         for r in rows:
             self.kv.lengths[r] += 1
         return self.buf.ids[:B]
@@ -237,8 +257,11 @@ class Qwen3Runtime:
         b.meta[:, :B].copy_(saved_meta)
         kv.seqlens.copy_(saved_len)
         g = torch.cuda.CUDAGraph()
+        lib = _lib.load()
+        n0 = lib.aacc_launch_count()
         with torch.cuda.graph(g):
             self._decode_body(B)
+        self.graph_launches[B] = int(lib.aacc_launch_count() - n0)
         b.meta[:, :B].copy_(saved_meta)
         kv.seqlens.copy_(saved_len)
         self._graphs[B] = g
@@ -249,6 +272,7 @@ class Qwen3Runtime:
         t = self._tok_host[:B]
         t.copy_(self.buf.ids[:B], non_blocking=True)
         torch.cuda.current_stream().synchronize()
+        self.d2h_bytes += B * 8
         return t.tolist()
 
     # ------------------------------------------------------------------ prefill
@@ -277,6 +301,7 @@ class Qwen3Runtime:
         smap = np.concatenate([kv.slot_mapping(r, 0, L) for r, L in zip(rows, lens)])
         host = torch.from_numpy(np.stack([flat, pos, smap])).pin_memory()
         meta = host.to(dev, non_blocking=True)
+        self.h2d_bytes += host.numel() * 8
         ids_d, pos_d, smap_d = meta[0], meta[1], meta[2]
         tokens = torch.empty(n, dtype=torch.int64, device=dev)
         V = self.vocab if self.comm.size == 1 else self.vocab_local
@@ -328,6 +353,7 @@ class Qwen3Runtime:
             m32 = np.concatenate([cu, np.asarray([s for _, s, _ in ch], dtype=np.int64)]).astype(np.int32)
             d64 = torch.from_numpy(m64).pin_memory().to(dev, non_blocking=True)
             d32 = torch.from_numpy(m32).pin_memory().to(dev, non_blocking=True)
+            self.h2d_bytes += m64.size * 8 + m32.size * 4
             seq_rows, last_idx = d64[:npc], d64[npc:]
             cu_q, ctx0 = d32[:npc + 1], d32[npc + 1:]
             max_q = max(e - s for _, s, e in ch)

@@ -1,0 +1,443 @@
+#!/usr/bin/env python3
+"""Benchmark: Qwen3 greedy generation throughput (output tok/s) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+                    [--workload cfg2|attn] [--small]
+
+Default workload: Qwen3-0.6B architecture, random-init
+bf16 weights, 256 sequences x 1024 uniform-random prompt tokens, 1024 greedy
+output tokens each (EOS ignored), continuous batching, paged KV block 256.
+One "step" is one whole generation job: the packed prefill of all 256
+prompts plus 1023 decode steps (256 x 1024 output tokens).
+
+* ``value``: device-timed throughput with the prompts already in HBM and the
+  decode loop replaying the captured decode-step graph (next tokens stay on
+  the device); CUDA events on the launching stream, max over ranks.
+* ``e2e``: the same job through the public API ``LLM.generate_ids`` with
+  host token lists in and out (pinned H2D staging each step, a D2H read of
+  every step's tokens).
+* ``roofline``: the dominant kernel, the paged decode attention, timed with
+  CUDA events on the real end-of-job KV state (algorithmic bytes = K+V of
+  every context token + q in + o out + block-table reads).
+* ``cpu_baseline``: the CPU oracle (a restatement of the reference's own
+  PyTorch code path, bf16 on all host cores) over a bounded sample of the
+  same workload.
+
+Under torchrun (N>1) every rank runs an independent replica (DP, weak
+scaling); ``value`` is the total over ranks divided by the slowest rank.
+``--impl reference`` times the reference's CPU implementation (the oracle)
+on rank 0 only.  ``--workload attn`` is the decode-attention microbenchmark
+(BASELINE config 3).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        load = [s for s in sm if s > 300] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- workload
+def arch_0p6b():
+    from awesome_acceleration_b200.model.model import Qwen3Config
+    return Qwen3Config()
+
+
+def make_prompts(n, length, vocab, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, vocab, (n, length), generator=g).tolist()
+
+
+def attention_bytes(ctx, hq, hkv, bs):
+    """Algorithmic bytes of one paged decode-attention launch."""
+    ctx = np.asarray(ctx, dtype=np.int64)
+    return int(ctx.sum() * hkv * 128 * 2 * 2 + len(ctx) * hq * 128 * 2 * 2
+               + np.ceil(ctx / bs).sum() * 4)
+
+
+class Cfg2:
+    def __init__(self, args):
+        self.n_seqs = 32 if args.small else 256
+        self.prompt = 256 if args.small else 1024
+        self.out = 64 if args.small else 1024
+        self.seed = 1234 + args.rank
+
+
+def build_engine(cfg2, device, use_graphs=True):
+    from awesome_acceleration_b200.llm import LLM
+    cfg = arch_0p6b()
+    max_seq_len = cfg2.prompt + cfg2.out + 16
+    return LLM(None, max_num_seqs=cfg2.n_seqs, max_seq_len=max_seq_len, config=cfg, seed=cfg2.seed,
+               use_cuda_graphs=use_graphs, device=device)
+
+
+def device_job(llm, prompts, out_tokens):
+    """One whole job on device: prefill all prompts, then out_tokens-1 decode
+    steps replaying the decode graph.  Returns nothing (tokens stay on device)."""
+    rt = llm.model._rt()
+    kv = llm.model.kv
+    rows = list(range(len(prompts)))
+    for r in rows:  # all blocks the job needs, so no table upload mid-loop
+        kv.reserve(r, len(prompts[r]) + out_tokens)
+    kv.sync()
+    first = rt.prefill(prompts, rows)
+    rt.buf.ids[:len(rows)].copy_(first)
+    rt.load_positions_rows([len(p) for p in prompts], rows)
+    for _ in range(out_tokens - 1):
+        rt.decode_step(rows)
+    return rows
+
+
+def reset_job(llm, rows):
+    llm.model.kv.clear_all()
+
+
+def count_launches(llm, B, out_tokens, n_prompts):
+    from awesome_acceleration_b200 import kernels as Kk
+    return Kk.LAUNCHES
+
+
+def run_cfg2(args, device):
+    cfg2 = Cfg2(args)
+    torch.manual_seed(0)
+    llm = build_engine(cfg2, device)
+    vocab = llm.config.vocab_size
+    prompts = make_prompts(cfg2.n_seqs, cfg2.prompt, vocab, cfg2.seed)
+    from awesome_acceleration_b200 import _lib
+    lib = _lib.load()
+    rt = llm.model._rt()
+    stream = torch.cuda.current_stream()
+    # ---- warm-up (also captures the decode graph)
+    for _ in range(args.warmup):
+        rows = device_job(llm, prompts, cfg2.out)
+        torch.cuda.synchronize()
+        reset_job(llm, rows)
+    _lib.raise_on_device_error("warm-up")
+    # ---- timed region: K whole jobs, device-resident inputs
+    barrier(args)
+    torch.cuda.synchronize()
+    launches0 = lib.aacc_launch_count()
+    graph_before = rt.graph_replays
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    elapsed = 0.0
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        for _ in range(args.steps):
+            e0.record(stream)
+            rows = device_job(llm, prompts, cfg2.out)
+            e1.record(stream)
+            e1.synchronize()
+            elapsed += e0.elapsed_time(e1) / 1e3
+            reset_job(llm, rows)
+    torch.cuda.synchronize()
+    _lib.raise_on_device_error("timed region")
+    eager_launches = lib.aacc_launch_count() - launches0
+    replays = rt.graph_replays - graph_before
+    launches = eager_launches + replays * rt.graph_launches.get(cfg2.n_seqs, 0)
+    t_max = max_over_ranks(args, elapsed)
+    out_tok = cfg2.n_seqs * cfg2.out
+    value = args.world * out_tok * args.steps / t_max
+
+    # ---- roofline of the dominant kernel (paged decode attention) on the
+    # end-of-job KV state: every row at prompt + out - 1 cached tokens.
+    rows = device_job(llm, prompts, cfg2.out)
+    torch.cuda.synchronize()
+    roof = attention_roofline(llm, rows, reps=20)
+    reset_job(llm, rows)
+
+    # ---- e2e through the public API (host lists in/out)
+    torch.cuda.synchronize()
+    barrier(args)
+    h2d0, d2h0 = rt.h2d_bytes, rt.d2h_bytes
+    e0.record(stream)
+    t0 = time.perf_counter()
+    res = llm.generate_ids(prompts, max_tokens=cfg2.out, ignore_eos=True).result()
+    e1.record(stream)
+    e1.synchronize()
+    e2e_s = max(e0.elapsed_time(e1) / 1e3, time.perf_counter() - t0)
+    h2d = rt.h2d_bytes - h2d0
+    d2h = rt.d2h_bytes - d2h0
+    gen = sum(r.generated_tokens for r in res)
+    assert gen == out_tok, (gen, out_tok)
+    e2e_max = max_over_ranks(args, e2e_s)
+    llm.stop()
+    e2e = {"value": args.world * gen / e2e_max, "unit": "output tok/s",
+           "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "api": "LLM.generate_ids"}
+    step_ms = t_max / args.steps * 1e3
+    line = {
+        "metric": "output tok/s (Qwen3-0.6B, 256x1024 in / 1024 out, greedy)",
+        "value": round(value, 1), "unit": "output tok/s", "n_gpus": args.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(step_ms, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform random token ids, random-init weights)",
+        "config": {"workload": "cfg2: Qwen3-0.6B 256 seqs x 1024 prompt / 1024 output, greedy, ignore_eos, "
+                               "paged KV block 256" + (" [SMALL]" if args.small else ""),
+                   "global_batch": cfg2.n_seqs * args.world, "seq_len": cfg2.prompt + cfg2.out,
+                   "parallelism": f"dp{args.world}" if args.world > 1 else "single",
+                   "l2": "inputs larger than L2 (KV cache ~60 GB, weights 1.2 GB per step)"},
+        "e2e": e2e, "roofline": roof, "gpu_launches": int(launches), "clocks": clk.summary(),
+        "decode_tok_per_s_device": None,
+    }
+    return line
+
+
+def attention_roofline(llm, rows, reps=20):
+    """Time the paged decode attention alone on the real KV state (layer 0),
+    CUDA events on the launching stream."""
+    from awesome_acceleration_b200 import kernels as Kk
+    rt = llm.model._rt()
+    kv = llm.model.kv
+    B = len(rows)
+    ctx = [int(kv.lengths[r]) + 1 for r in rows]
+    q = torch.randn((B, rt.Hq, 128), dtype=torch.bfloat16, device=kv.k.device) / 11.3
+    out = torch.empty_like(q)
+    rows_d = torch.tensor(rows, dtype=torch.int64, device=kv.k.device)
+    stream = torch.cuda.current_stream()
+    times = []
+    # Rotate over layers so every launch reads cold KV (a layer's K+V exceeds L2).
+    for i in range(reps + 3):
+        layer = i % kv.num_layers
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        Kk.paged_decode_attention(q, kv.k[layer], kv.v[layer], kv.block_tables, rows_d, kv.seqlens, ctx_add=1,
+                                  scale=rt.scale, max_context=rt.max_context, workspace=rt.buf.attn_ws, out=out)
+        e1.record(stream)
+        e1.synchronize()
+        if i >= 3:
+            times.append(e0.elapsed_time(e1) / 1e3)
+    t = statistics.mean(times)
+    byts = attention_bytes(ctx, rt.Hq, rt.Hkv, kv.block_size)
+    pk, kind = peaks()
+    ach = byts / t / 1e9
+    return {"kernel": "paged_decode_kernel (+decode_combine_kernel)", "bound": "hbm",
+            "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(ach / pk["hbm_gbs"], 3),
+            "peak_kind": kind, "traffic": None, "bytes_per_launch": byts, "us_per_launch": round(t * 1e6, 2),
+            "state": f"B={B}, ctx={min(ctx)}..{max(ctx)}"}
+
+
+# --------------------------------------------------------------------------- attn microbench (config 3)
+def run_attn(args, device):
+    from awesome_acceleration_b200 import _lib, kernels as Kk
+    g = torch.Generator().manual_seed(7)
+    B, hq, hkv, bs = 256, 16, 8, 256
+    nb = 4096 if args.small else 65536
+    lo, hi = 512, 4096
+    ctx = torch.randint(lo, hi + 1, (B,), generator=g).tolist()
+    maxb = (hi + bs - 1) // bs
+    perm = torch.randperm(nb, generator=g)
+    bt = torch.full((B, maxb), -1, dtype=torch.int32)
+    it = 0
+    for b, c in enumerate(ctx):
+        n = (c + bs - 1) // bs
+        bt[b, :n] = perm[it:it + n].int()
+        it += n
+    kc = torch.empty((nb, hkv, bs, 128), dtype=torch.bfloat16, device=device)
+    vc = torch.empty_like(kc)
+    kc.normal_()
+    vc.normal_()
+    q = torch.randn((B, hq, 128), dtype=torch.bfloat16, device=device) / 128 ** 0.5
+    seqlens = torch.tensor(ctx, dtype=torch.int32, device=device) - 1
+    rows = torch.arange(B, dtype=torch.int64, device=device)
+    btd = bt.to(device)
+    ws = torch.empty(Kk.decode_workspace_bytes(B, hq, maxb * bs), dtype=torch.uint8, device=device)
+    out = torch.empty_like(q)
+    # slot mapping of the new token (1 per sequence) + its store, as in a decode step
+    stream = torch.cuda.current_stream()
+
+    def call():
+        Kk.paged_decode_attention(q, kc, vc, btd, rows, seqlens, ctx_add=1, scale=128 ** -0.5,
+                                  max_context=maxb * bs, workspace=ws, out=out)
+
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    flush = torch.empty(256 * 1024 * 1024 // 2, dtype=torch.bfloat16, device=device)
+    times = []
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        for _ in range(args.steps):
+            flush.zero_()  # > L2: every launch reads K/V from HBM
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            call()
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1) / 1e3)
+    _lib.raise_on_device_error("attn bench")
+    t = statistics.mean(times)
+    byts = attention_bytes(ctx, hq, hkv, bs)
+    pk, kind = peaks()
+    ach = byts / t / 1e9
+    return {"metric": "paged decode-attention HBM GB/s (B=256, Hq16/Hkv8, ctx U[512,4096])",
+            "value": round(ach, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t * 1e3, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "cfg3 decode-attention microbenchmark", "pool_blocks": nb,
+                       "l2": "flushed between launches"},
+            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(ach / pk["hbm_gbs"], 3), "traffic": None, "peak_kind": kind},
+            "gpu_launches": 2 * args.steps, "clocks": clk.summary()}
+
+
+# --------------------------------------------------------------------------- CPU baseline (oracle)
+def cpu_sample(n_seqs=4, prompt=1024, out=8, seed=99):
+    """The reference's CPU code path (restated by the oracle, bf16, all host
+    cores) on a bounded sample of the cfg2 workload: n_seqs prompts of the
+    same length, prefill + (out - 1) decode steps.  Returns (tok/s, info)."""
+    from oracle.qwen3_oracle import Qwen3Oracle, run_greedy
+    from oracle.weights import QWEN3_0_6B, init_weights
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    sd = init_weights(QWEN3_0_6B, seed)
+    orc = Qwen3Oracle(QWEN3_0_6B, sd, torch.bfloat16, num_slots=n_seqs, max_seq_len=prompt + out + 8)
+    prompts = make_prompts(n_seqs, prompt, QWEN3_0_6B.vocab_size, seed)
+    t0 = time.perf_counter()
+    run_greedy(orc, prompts, out - 1)
+    dt = time.perf_counter() - t0
+    return n_seqs * out / dt, {"cores": cores,
+                                "sample": f"{n_seqs} seqs x {prompt} prompt tokens, prefill + {out - 1} decode "
+                                          f"steps ({n_seqs * out} output tokens, {dt:.1f} s), bf16"}
+
+
+def run_reference(args):
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, info = cpu_sample()
+        if i >= args.warmup:
+            vals.append(v)
+    v = statistics.mean(vals)
+    return {"impl": "reference", "metric": "output tok/s (Qwen3-0.6B, 256x1024 in / 1024 out, greedy)",
+            "value": round(v, 3), "unit": "output tok/s", "n_gpus": args.world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "cfg2 (bounded CPU sample)", "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(v, 3), "unit": "output tok/s", "cores": info["cores"], "kind": "port",
+                             "sample": info["sample"]},
+            "e2e": {"value": round(v, 3), "unit": "output tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+# --------------------------------------------------------------------------- dist plumbing
+def barrier(args):
+    if args.world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(args, x: float) -> float:
+    if args.world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "attn"])
+    ap.add_argument("--small", action="store_true", help="small case for profiler captures")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.world = int(os.environ.get("WORLD_SIZE", "1"))
+    args.rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if args.rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if args.world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                             device_id=device)
+    try:
+        line = run_attn(args, device) if args.workload == "attn" else run_cfg2(args, device)
+        if args.rank == 0 and args.workload == "cfg2" and not args.no_cpu_baseline:
+            v, info = cpu_sample()
+            line["cpu_baseline"] = {"value": round(v, 3), "unit": "output tok/s", "cores": info["cores"],
+                                    "kind": "port", "sample": info["sample"]}
+        if args.rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if args.world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

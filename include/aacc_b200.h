@@ -40,6 +40,9 @@ extern "C" {
 /* ---- library / error plumbing ------------------------------------------ */
 int aacc_version(void);
 const char* aacc_last_error(void);
+/* Kernels this library has launched (or recorded into a graph capture) in
+ * this process; used for launch accounting by the benchmark. */
+unsigned long long aacc_launch_count(void);
 /* Copy the device error word of the current device into *out (synchronous). */
 int aacc_get_device_error(unsigned* out);
 int aacc_clear_device_error(void);

@@ -35,8 +35,8 @@ def attend(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
     vf = v.float().repeat_interleave(G, dim=1)
     s = torch.einsum("qhd,khd->hqk", qf, kf) * scale
     if causal:
-        i = torch.arange(Lq).unsqueeze(1)
-        j = torch.arange(Lk).unsqueeze(0)
+        i = torch.arange(Lq, device=q.device).unsqueeze(1)
+        j = torch.arange(Lk, device=q.device).unsqueeze(0)
         s = s.masked_fill(j > i + (Lk - Lq), float("-inf"))
     m = s.amax(dim=-1, keepdim=True)
     p = torch.exp(s - m)

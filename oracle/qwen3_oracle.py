@@ -50,7 +50,7 @@ def rope_cos_sin(positions: torch.Tensor, dim: int, theta: float, dtype) -> tupl
     positions and the frequencies are therefore bf16 (position 257 becomes
     256, ...), and ``t * inv_freq`` and cos/sin round to bf16.  In fp32 the
     same code is plain fp32."""
-    inv = rope_inv_freq(dim, theta).to(dtype)
+    inv = rope_inv_freq(dim, theta).to(dtype).to(positions.device)
     t = positions.to(dtype)
     freqs = t.unsqueeze(-1) * inv
     emb = torch.cat((freqs, freqs), dim=-1)
@@ -79,11 +79,12 @@ class Qwen3Oracle:
     model/model.py:324-336)."""
 
     def __init__(self, arch: Qwen3Arch, state_dict: dict, dtype=torch.float32,
-                 num_slots: int = 4, max_seq_len: int = 512):
+                 num_slots: int = 4, max_seq_len: int = 512, device="cpu"):
         self.arch = arch
         self.dtype = dtype
         self.max_seq_len = max_seq_len
-        self.w = {k: v.to(dtype) for k, v in state_dict.items()}
+        self.device = torch.device(device)
+        self.w = {k: v.to(device=self.device, dtype=dtype) for k, v in state_dict.items()}
         a = arch
         self.q_size = a.num_attention_heads * a.head_dim
         self.kv_size = a.num_key_value_heads * a.head_dim
@@ -95,8 +96,8 @@ class Qwen3Oracle:
                                         self.w[p + "v_proj.weight"]], 0))
         self.lm_head = self.w.get("lm_head.weight", self.w["model.embed_tokens.weight"])
         shape = (num_slots, max_seq_len, a.num_key_value_heads, a.head_dim)
-        self.k_cache = [torch.zeros(shape, dtype=dtype) for _ in range(a.num_hidden_layers)]
-        self.v_cache = [torch.zeros(shape, dtype=dtype) for _ in range(a.num_hidden_layers)]
+        self.k_cache = [torch.zeros(shape, dtype=dtype, device=self.device) for _ in range(a.num_hidden_layers)]
+        self.v_cache = [torch.zeros(shape, dtype=dtype, device=self.device) for _ in range(a.num_hidden_layers)]
         self.seqlens = torch.zeros(num_slots, dtype=torch.int32)
 
     def _lw(self, i, name):
@@ -125,12 +126,13 @@ class Qwen3Oracle:
         eps = a.rms_norm_eps
         lens = [len(s) for s in sequences]
         T = sum(lens)
-        flat = torch.tensor([t for s in sequences for t in s], dtype=torch.long)
+        dev = self.device
+        flat = torch.tensor([t for s in sequences for t in s], dtype=torch.long, device=dev)
         cu = [0]
         for n in lens:
             cu.append(cu[-1] + n)
         cu_t = torch.tensor(cu, dtype=torch.int32)
-        pos = torch.cat([torch.arange(n) for n in lens])
+        pos = torch.cat([torch.arange(n) for n in lens]).to(dev)
         cos, sin = rope_cos_sin(pos, a.head_dim, a.rope_theta, self.dtype)
         cos, sin = cos.unsqueeze(1), sin.unsqueeze(1)
         hidden = self.w["model.embed_tokens.weight"][flat]
@@ -151,7 +153,7 @@ class Qwen3Oracle:
         for s_i, slot in enumerate(slots):
             self.seqlens[slot] = lens[s_i]
         hidden = rms_norm(hidden, self.w["model.norm.weight"], eps)
-        return hidden[torch.tensor(cu[1:]) - 1]
+        return hidden[torch.tensor(cu[1:], device=dev) - 1]
 
     def prefill(self, sequences: list[list[int]], slots: list[int]) -> torch.Tensor:
         """llm.py:116-208 -> logits [n, V]."""
@@ -161,8 +163,8 @@ class Qwen3Oracle:
         """model/model.py:279-286 decode branch: [B, H] final-normed hidden."""
         a = self.arch
         eps = a.rms_norm_eps
-        ids = torch.tensor(tokens, dtype=torch.long)
-        pos = torch.tensor(positions, dtype=torch.long)
+        ids = torch.tensor(tokens, dtype=torch.long, device=self.device)
+        pos = torch.tensor(positions, dtype=torch.long, device=self.device)
         cos, sin = rope_cos_sin(pos, a.head_dim, a.rope_theta, self.dtype)
         cos, sin = cos.unsqueeze(1), sin.unsqueeze(1)
         hidden = self.w["model.embed_tokens.weight"][ids]

@@ -1,0 +1,322 @@
+"""Per-kernel parity of the sm_100a kernels against the CPU oracle, called
+through the C ABI (awesome_acceleration_b200.kernels -> libaacc_b200.so)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle.attention import attend
+from oracle.qwen3_oracle import apply_rope, rms_norm, rope_cos_sin
+
+pytestmark = pytest.mark.gpu
+BF = torch.bfloat16
+
+
+def K():
+    from awesome_acceleration_b200 import kernels
+    return kernels
+
+
+def dev_err():
+    from awesome_acceleration_b200 import _lib
+    return _lib.device_error()
+
+
+def clear_err():
+    from awesome_acceleration_b200 import _lib
+    _lib.clear_device_error()
+
+
+def rand_pool(nb, hkv, bs, gen, dev):
+    k = torch.randn((nb, hkv, bs, 128), generator=gen).to(BF).to(dev)
+    v = torch.randn((nb, hkv, bs, 128), generator=gen).to(BF).to(dev)
+    return k, v
+
+
+def block_tables_for(ctx, bs, nb, gen, max_blocks=None):
+    need = [(c + bs - 1) // bs for c in ctx]
+    mb = max_blocks or max(need)
+    perm = torch.randperm(nb, generator=gen).tolist()
+    assert sum(need) <= nb
+    bt = torch.full((len(ctx), mb), -1, dtype=torch.int32)
+    it = 0
+    for i, n in enumerate(need):
+        bt[i, :n] = torch.tensor(perm[it:it + n], dtype=torch.int32)
+        it += n
+    return bt
+
+
+def gather_kv(pool, bt_row, length, bs):
+    pos = torch.arange(length)
+    blk = bt_row.long()[pos // bs]
+    return pool[blk, :, pos % bs]  # [length, Hkv, 128]
+
+
+# --------------------------------------------------------------------------- KV store
+def test_kv_store_bit_exact(cuda):
+    g = torch.Generator().manual_seed(0)
+    nb, hkv, bs, T = 12, 4, 64, 300
+    kc = torch.full((nb, hkv, bs, 128), 7.0, dtype=BF, device=cuda)
+    vc = torch.full((nb, hkv, bs, 128), -3.0, dtype=BF, device=cuda)
+    k = torch.randn((T, hkv * 128 + 64), generator=g).to(BF)  # row stride > row width
+    v = torch.randn((T, hkv * 128), generator=g).to(BF)
+    slots = torch.randperm(nb * bs, generator=g)[:T]
+    slots[::17] = -1  # skipped rows
+    clear_err()
+    K().kv_store(k.to(cuda)[:, :hkv * 128], v.to(cuda), slots.to(cuda), kc, vc)
+    torch.cuda.synchronize()
+    assert dev_err() == 0
+    kc_h, vc_h = kc.cpu(), vc.cpu()
+    written = torch.zeros(nb * bs, dtype=torch.bool)
+    for t in range(T):
+        s = int(slots[t])
+        if s < 0:
+            continue
+        written[s] = True
+        assert torch.equal(kc_h[s // bs, :, s % bs], k[t, :hkv * 128].view(hkv, 128))
+        assert torch.equal(vc_h[s // bs, :, s % bs], v[t].view(hkv, 128))
+    untouched = (~written).nonzero().flatten()
+    assert (kc_h.permute(0, 2, 1, 3).reshape(nb * bs, -1)[untouched] == 7.0).all()
+    assert (vc_h.permute(0, 2, 1, 3).reshape(nb * bs, -1)[untouched] == -3.0).all()
+
+
+def test_kv_store_rejects_out_of_pool_slot(cuda):
+    nb, hkv, bs = 2, 1, 64
+    kc = torch.zeros((nb, hkv, bs, 128), dtype=BF, device=cuda)
+    vc = torch.zeros_like(kc)
+    k = torch.ones((2, 128), dtype=BF, device=cuda)
+    slots = torch.tensor([5, nb * bs + 3], dtype=torch.int64, device=cuda)
+    clear_err()
+    K().kv_store(k, k, slots, kc, vc)
+    torch.cuda.synchronize()
+    assert dev_err() & 2  # ERR_SLOT_OOB, access skipped
+    assert kc.float().sum().item() == 128.0
+    clear_err()
+
+
+def test_decode_slot_mapping_and_advance(cuda):
+    bs, nb = 64, 16
+    g = torch.Generator().manual_seed(1)
+    ctx = [1, 63, 64, 65, 200]
+    bt = block_tables_for([c + 1 for c in ctx], bs, nb, g, max_blocks=6)
+    rows = torch.tensor([4, 0, 2, 1, 3], dtype=torch.int64)
+    seqlens = torch.zeros(5, dtype=torch.int32)
+    for b, r in enumerate(rows.tolist()):
+        seqlens[r] = ctx[b]
+    bt_rows = torch.full((5, 6), -1, dtype=torch.int32)
+    for b, r in enumerate(rows.tolist()):
+        bt_rows[r] = bt[b]
+    out = torch.empty(5, dtype=torch.int64, device=cuda)
+    sl = seqlens.to(cuda)
+    pos = torch.arange(5, dtype=torch.int64, device=cuda)
+    K().decode_slot_mapping(rows.to(cuda), sl, bt_rows.to(cuda), bs, nb, out)
+    K().advance_seqlens(rows.to(cuda), sl, pos)
+    torch.cuda.synchronize()
+    for b, r in enumerate(rows.tolist()):
+        n = ctx[b]
+        assert int(out[b]) == int(bt_rows[r, n // bs]) * bs + n % bs
+        assert int(sl[r]) == n + 1
+    assert pos.tolist() == [1, 2, 3, 4, 5]
+
+
+# --------------------------------------------------------------------------- decode attention
+@pytest.mark.parametrize("G,hkv", [(1, 2), (2, 8), (4, 2), (8, 1)])
+def test_paged_decode_attention(cuda, G, hkv):
+    g = torch.Generator().manual_seed(10 + G)
+    bs = 256
+    ctx = [1, 2, 63, 64, 65, 255, 256, 257, 511, 1000, 2049, 4096]
+    B = len(ctx)
+    hq = G * hkv
+    need = sum((c + bs - 1) // bs for c in ctx)
+    nb = need + 7
+    kp, vp = rand_pool(nb, hkv, bs, g, "cpu")
+    bt = block_tables_for(ctx, bs, nb, g)
+    rows = torch.randperm(B, generator=g)  # rows are a permutation of the batch
+    bt_rows = torch.full_like(bt, -1)
+    seqlens = torch.zeros(B, dtype=torch.int32)
+    for b in range(B):
+        bt_rows[rows[b]] = bt[b]
+        seqlens[rows[b]] = ctx[b] - 1  # ctx_add = 1: attend over seqlens + 1
+    q = (torch.randn((B, hq, 128), generator=g) / math.sqrt(128)).to(BF)
+    scale = 128 ** -0.5
+    max_ctx = bt.shape[1] * bs
+    ws = torch.empty(K().decode_workspace_bytes(B, hq, max_ctx, 64), dtype=torch.uint8, device=cuda)
+    clear_err()
+    for split in (0, 64, 512):
+        out = K().paged_decode_attention(q.to(cuda), kp.to(cuda), vp.to(cuda), bt_rows.to(cuda),
+                                         rows.to(cuda), seqlens.to(cuda), ctx_add=1, scale=scale,
+                                         max_context=max_ctx, workspace=ws, split_tokens=split)
+        torch.cuda.synchronize()
+        assert dev_err() == 0
+        out = out.cpu().float()
+        for b in range(B):
+            kk = gather_kv(kp, bt[b], ctx[b], bs)
+            vv = gather_kv(vp, bt[b], ctx[b], bs)
+            ref = attend(q[b:b + 1], kk, vv, scale, False)[0].float()
+            err = (out[b] - ref).abs().max().item()
+            assert err <= 2e-2, f"split {split} row {b} ctx {ctx[b]}: max-abs {err}"
+
+
+# --------------------------------------------------------------------------- prefill attention
+@pytest.mark.parametrize("G,hkv", [(2, 2), (4, 2), (1, 3)])
+def test_prefill_attention_chunked(cuda, G, hkv):
+    g = torch.Generator().manual_seed(20 + G)
+    bs = 256
+    # (context already cached, query chunk length)
+    pieces = [(0, 1), (0, 5), (0, 64), (0, 130), (100, 30), (256, 257), (500, 64), (0, 700)]
+    S = len(pieces)
+    hq = G * hkv
+    tot = [c + n for c, n in pieces]
+    nb = sum((t + bs - 1) // bs for t in tot) + 3
+    kp, vp = rand_pool(nb, hkv, bs, g, "cpu")
+    bt = block_tables_for(tot, bs, nb, g)
+    T = sum(n for _, n in pieces)
+    q = (torch.randn((T, hq, 128), generator=g)).to(BF)
+    cu = torch.tensor([0] + np.cumsum([n for _, n in pieces]).tolist(), dtype=torch.int32)
+    ctx0 = torch.tensor([c for c, _ in pieces], dtype=torch.int32)
+    rows = torch.arange(S, dtype=torch.int64)
+    scale = 128 ** -0.5
+    clear_err()
+    out = K().prefill_attention(q.to(cuda), kp.to(cuda), vp.to(cuda), bt.to(cuda), rows.to(cuda), cu.to(cuda),
+                                ctx0.to(cuda), max_q_len=max(n for _, n in pieces), scale=scale)
+    torch.cuda.synchronize()
+    assert dev_err() == 0
+    out = out.cpu().float()
+    for s, (c, n) in enumerate(pieces):
+        kk = gather_kv(kp, bt[s], c + n, bs)
+        vv = gather_kv(vp, bt[s], c + n, bs)
+        ref = attend(q[cu[s]:cu[s + 1]], kk, vv, scale, True).float()
+        err = (out[cu[s]:cu[s + 1]] - ref).abs().max().item()
+        assert err <= 2e-2, f"piece {s} ({c},{n}): max-abs {err}"
+
+
+# --------------------------------------------------------------------------- norms
+@pytest.mark.parametrize("H", [1024, 4096, 5120])
+def test_rmsnorm_family(cuda, H):
+    g = torch.Generator().manual_seed(H)
+    T, eps = 37, 1e-6
+    x = (torch.randn((T, H), generator=g) * 3).to(BF)
+    d = torch.randn((T, H), generator=g).to(BF)
+    w = (1 + 0.1 * torch.randn(H, generator=g)).to(BF)
+    y = K().rmsnorm(x.to(cuda), w.to(cuda), eps).cpu()
+    ref = rms_norm(x, w, eps)
+    assert (y.float() - ref.float()).abs().max().item() <= 2 ** -6 * 4  # <= 1 bf16 ulp at |y| < 4
+    assert (y == ref).float().mean().item() > 0.999
+    res = x.to(cuda).clone()
+    y2 = K().add_rmsnorm(d.to(cuda), res, w.to(cuda), eps).cpu()
+    r_ref = x + d
+    assert torch.equal(res.cpu(), r_ref)
+    ref2 = rms_norm(r_ref, w, eps)
+    assert (y2 == ref2).float().mean().item() > 0.999
+    V = 1000
+    table = torch.randn((V, H), generator=g).to(BF)
+    ids = torch.randint(0, V, (T,), generator=g)
+    res3 = torch.empty((T, H), dtype=BF, device=cuda)
+    y3 = torch.empty((T, H), dtype=BF, device=cuda)
+    K().embed_rmsnorm(ids.to(cuda), table.to(cuda), w.to(cuda), eps, res3, y3)
+    assert torch.equal(res3.cpu(), table[ids])
+    assert (y3.cpu() == rms_norm(table[ids], w, eps)).float().mean().item() > 0.999
+
+
+# --------------------------------------------------------------------------- GEMMs
+def bf16_linear_ref(x, w):
+    return (x.float() @ w.float().t())
+
+
+@pytest.mark.parametrize("M", [1, 5, 128, 129, 256, 300, 1111])
+@pytest.mark.parametrize("N,Kd", [(1024, 2048), (384, 1024), (4096, 64)])
+def test_gemm(cuda, M, N, Kd):
+    g = torch.Generator().manual_seed(M * 7 + N)
+    x = torch.randn((M, Kd), generator=g).to(BF)
+    w = (torch.randn((N, Kd), generator=g) * 0.02).to(BF)
+    out = K().gemm(x.to(cuda), w.to(cuda)).cpu().float()
+    ref = bf16_linear_ref(x, w)
+    err = (out - ref).abs().max().item()
+    tol = 1e-2 * ref.abs().max().item() + 1e-3
+    assert err <= tol, f"max-abs {err} > {tol}"
+
+
+@pytest.mark.parametrize("M", [3, 256, 700])
+def test_gemm_silu_mul(cuda, M):
+    from awesome_acceleration_b200.runtime import interleave_gate_up
+    g = torch.Generator().manual_seed(M)
+    H, I = 1024, 3072
+    x = torch.randn((M, H), generator=g).to(BF)
+    wg = (torch.randn((I, H), generator=g) * 0.05).to(BF)
+    wu = (torch.randn((I, H), generator=g) * 0.05).to(BF)
+    wgu = interleave_gate_up(wg, wu).contiguous()
+    out = K().gemm_silu_mul(x.to(cuda), wgu.to(cuda)).cpu().float()
+    ref = (F.silu(F.linear(x, wg)) * F.linear(x, wu)).float()  # reference rounding points (bf16 eager)
+    err = (out - ref).abs().max().item()
+    assert err <= 2e-2 * ref.abs().max().item() + 1e-3, err
+
+
+@pytest.mark.parametrize("M,hq,hkv", [(1, 16, 8), (40, 16, 8), (260, 8, 2), (1300, 4, 2)])
+def test_qkv_norm_rope_store(cuda, M, hq, hkv):
+    g = torch.Generator().manual_seed(M + hq)
+    H, bs, eps = 1024, 256, 1e-6
+    x = torch.randn((M, H), generator=g).to(BF)
+    wqkv = (torch.randn(((hq + 2 * hkv) * 128, H), generator=g) * 0.05).to(BF)
+    qn = (1 + 0.1 * torch.randn(128, generator=g)).to(BF)
+    kn = (1 + 0.1 * torch.randn(128, generator=g)).to(BF)
+    pos = torch.randint(0, 5000, (M,), generator=g)
+    nb = (M + bs - 1) // bs + 2
+    slots = torch.randperm(nb * bs, generator=g)[:M]
+    from awesome_acceleration_b200.runtime import rope_table
+    table = rope_table(8192, 128, 1e6, cuda)
+    kc = torch.zeros((nb, hkv, bs, 128), dtype=BF, device=cuda)
+    vc = torch.zeros_like(kc)
+    clear_err()
+    q = K().qkv_norm_rope_store(x.to(cuda), wqkv.to(cuda), qn.to(cuda), kn.to(cuda), eps, pos.to(cuda), table,
+                                slots.to(cuda), kc, vc, hq)
+    torch.cuda.synchronize()
+    assert dev_err() == 0
+    # Oracle chain: F.linear -> q/k RMSNorm -> RoPE (reference rounding points).
+    qkv = F.linear(x, wqkv)
+    qr = rms_norm(qkv[:, :hq * 128].view(M, hq, 128), qn, eps)
+    kr = rms_norm(qkv[:, hq * 128:(hq + hkv) * 128].view(M, hkv, 128), kn, eps)
+    vr = qkv[:, (hq + hkv) * 128:].view(M, hkv, 128)
+    cos, sin = rope_cos_sin(pos, 128, 1e6, BF)
+    qr, kr = apply_rope(qr, kr, cos.unsqueeze(1), sin.unsqueeze(1))
+    assert (q.cpu().float() - qr.float()).abs().max().item() <= 0.1
+    assert (q.cpu() == qr).float().mean().item() > 0.95
+    kc_h, vc_h = kc.cpu(), vc.cpu()
+    ks = kc_h[slots // bs, :, slots % bs]
+    vs = vc_h[slots // bs, :, slots % bs]
+    assert (ks.float() - kr.float()).abs().max().item() <= 0.1
+    assert (ks == kr).float().mean().item() > 0.95
+    # V is the bf16-rounded projection itself: equal up to one bf16 ulp.
+    mag = torch.maximum(vs.float().abs(), vr.float().abs())
+    assert ((vs.float() - vr.float()).abs() <= mag * 2 ** -7 + 1e-6).all()
+
+
+@pytest.mark.parametrize("M,V", [(1, 151936), (7, 4096), (256, 151936), (300, 18992)])
+def test_lm_head_argmax(cuda, M, V):
+    g = torch.Generator().manual_seed(M + V)
+    H = 1024
+    x = torch.randn((M, H), generator=g).to(BF)
+    w = (torch.randn((V, H), generator=g) * 0.02).to(BF)
+    tokens = torch.empty(M, dtype=torch.int64, device=cuda)
+    best = torch.empty(M, dtype=torch.float32, device=cuda)
+    logits = torch.empty((M, V), dtype=BF, device=cuda)
+    ws = torch.empty(K().lm_head_workspace_bytes(M, V), dtype=torch.uint8, device=cuda)
+    K().lm_head_argmax(x.to(cuda), w.to(cuda), tokens, ws, logits=logits, best_val=best, vocab_offset=0)
+    torch.cuda.synchronize()
+    lg = logits.cpu()
+    # Fused argmax agrees exactly with torch.argmax over the kernel's own bf16 logits.
+    assert torch.equal(tokens.cpu(), lg.argmax(-1))
+    assert torch.equal(best.cpu(), lg.float().max(-1).values)
+    # And the logits agree with a CPU bf16 linear within bf16 tolerance.
+    ref = F.linear(x, w).float()
+    assert (lg.float() - ref).abs().max().item() <= 2e-2
+    t2 = K().argmax_rows(logits)
+    assert torch.equal(t2.cpu(), tokens.cpu())
+
+
+def test_argmax_merge_ties_lowest_index(cuda):
+    val = torch.tensor([[1.0, 5.0], [3.0, 5.0], [3.0, 2.0]], device=cuda)      # [shards=3, M=2]
+    idx = torch.tensor([[10, 7], [20, 3], [5, 1]], dtype=torch.int64, device=cuda)
+    out = K().argmax_merge(val, idx)
+    assert out.tolist() == [5, 3]
