@@ -1,0 +1,254 @@
+"""Tensor-parallel Qwen3 with the reference's interface on B200 kernels.
+
+Mirrors yijichar/AWesome_ACceleration model/model_tp.py: heads and MLP
+columns are sharded Megatron-style (QKVParallelLinear / ColumnParallel for
+gate/up, RowParallel for o_proj/down), every rank holds only its KV heads,
+and ``_convert_to_tp`` slices a full state dict exactly like the reference
+(:478-567).
+
+Differences (new capabilities behind the same interface):
+  * the lm_head is vocab-parallel: rank r scores vocab rows
+    [r*V/t, (r+1)*V/t) and the greedy token comes from an all-gather of every
+    rank's (max logit, id) + a merge kernel, instead of rank 0 computing the
+    full logits (model/model_tp.py:365-381); ``forward`` still returns full
+    logits (all-gathered) for API compatibility;
+  * the RowParallel all-reduces run inside the CUDA-graph-captured decode
+    step, followed by the fused residual-add + RMSNorm kernel.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from ..kv_cache import PagedKVCache
+from ..runtime import LayerWeights, Qwen3Runtime, TPComm, interleave_gate_up, rope_table
+from .distributed import (get_tp_group, get_tp_rank, get_tp_world_size, split_tensor_along_dim,
+                          tensor_model_parallel_all_gather)
+from .model import Qwen3Config, RMSNorm, RotaryEmbedding
+from .parallel_layers import ColumnParallelLinear, QKVParallelLinear, RowParallelLinear, qkv_rank_rows
+
+
+class AttentionTP(nn.Module):
+    """model/model_tp.py:112-176."""
+
+    def __init__(self, config: Qwen3Config):
+        super().__init__()
+        self.hidden_size = config.hidden_size
+        self.num_heads = config.num_attention_heads
+        self.num_kv_heads = config.num_key_value_heads
+        self.head_dim = config.head_dim
+        self.tp_size = get_tp_world_size()
+        assert self.num_heads % self.tp_size == 0, \
+            f"num_heads ({self.num_heads}) must be divisible by tp_size ({self.tp_size})"
+        assert self.num_kv_heads % self.tp_size == 0, \
+            f"num_kv_heads ({self.num_kv_heads}) must be divisible by tp_size ({self.tp_size})"
+        self.num_heads_per_partition = self.num_heads // self.tp_size
+        self.num_kv_heads_per_partition = self.num_kv_heads // self.tp_size
+        self.num_kv_groups = self.num_heads_per_partition // self.num_kv_heads_per_partition
+        self._q_size = self.num_heads * self.head_dim
+        self._kv_size = self.num_kv_heads * self.head_dim
+        self.q_norm = RMSNorm(self.head_dim, eps=config.rms_norm_eps)
+        self.k_norm = RMSNorm(self.head_dim, eps=config.rms_norm_eps)
+        self._qkv_proj = QKVParallelLinear(self.hidden_size, self.num_heads, self.num_kv_heads, self.head_dim)
+        self.o_proj = RowParallelLinear(self._q_size, self.hidden_size, bias=False, input_is_parallel=True)
+        self.rotary_emb = RotaryEmbedding(self.head_dim, config.max_position_embeddings, config.rope_theta)
+        self.scaling = self.head_dim ** -0.5
+        self._kv_cache = None
+        self._v_cache = None
+        self._cache_seqlens = None
+
+
+class MLPTP(nn.Module):
+    """model/model_tp.py:263-299."""
+
+    def __init__(self, config: Qwen3Config):
+        super().__init__()
+        self.gate_proj = ColumnParallelLinear(config.hidden_size, config.intermediate_size, bias=False)
+        self.up_proj = ColumnParallelLinear(config.hidden_size, config.intermediate_size, bias=False)
+        self.down_proj = RowParallelLinear(config.intermediate_size, config.hidden_size, bias=False)
+        self.act_fn = nn.SiLU()
+        self._gate_up = None
+
+    def fuse_gate_up(self):
+        with torch.no_grad():
+            self._gate_up = interleave_gate_up(self.gate_proj.weight, self.up_proj.weight).contiguous()
+
+
+class TransformerBlockTP(nn.Module):
+    def __init__(self, config: Qwen3Config):
+        super().__init__()
+        self.input_layernorm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+        self.self_attn = AttentionTP(config)
+        self.post_attention_layernorm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+        self.mlp = MLPTP(config)
+
+
+class Qwen3ModelTP(nn.Module):
+    """Replicated embedding (model/model_tp.py:327-349)."""
+
+    def __init__(self, config: Qwen3Config):
+        super().__init__()
+        self.config = config
+        self.embed_tokens = nn.Embedding(config.vocab_size, config.hidden_size)
+        self.layers = nn.ModuleList([TransformerBlockTP(config) for _ in range(config.num_hidden_layers)])
+        self.norm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+
+
+class Qwen3ForCausalLMTP(nn.Module):
+    """model/model_tp.py:352-567 on the B200 hot path."""
+
+    def __init__(self, config: Qwen3Config):
+        super().__init__()
+        self.config = config
+        self.model = Qwen3ModelTP(config)
+        self.lm_head = None if config.tie_word_embeddings else nn.Linear(config.hidden_size, config.vocab_size,
+                                                                        bias=False)
+        self.tp_size, self.tp_rank = get_tp_world_size(), get_tp_rank()
+        if config.vocab_size % self.tp_size:
+            raise ValueError(f"vocab_size {config.vocab_size} must be divisible by tp_size {self.tp_size}")
+        self.kv: PagedKVCache | None = None
+        self.runtime: Qwen3Runtime | None = None
+        self.rope = None
+        self.max_batch = 256
+        self.use_cuda_graphs = True
+        self.prefill_chunk_tokens = 32768
+        self._lm_shard = None
+
+    # ------------------------------------------------------------------ setup
+    def fuse_qkv(self):
+        """QKV is fused by construction (QKVParallelLinear); fuse gate/up and
+        cut this rank's vocab shard of the lm_head."""
+        for layer in self.model.layers:
+            layer.mlp.fuse_gate_up()
+        w = self.model.embed_tokens.weight if self.lm_head is None else self.lm_head.weight
+        self._lm_shard = split_tensor_along_dim(w.data, self.tp_size, dim=0)
+        self.runtime = None
+
+    def init_kv_cache(self, num_slots: int, max_seq_len: int, device, dtype, *, block_size: int = 256,
+                      num_blocks: int | None = None, max_batch: int | None = None):
+        """Per-rank KV heads (model/model_tp.py:410-426), paged."""
+        if dtype != torch.bfloat16:
+            raise ValueError("the B200 hot path computes in bf16")
+        cfg = self.config
+        self.kv = PagedKVCache(cfg.num_hidden_layers, cfg.num_key_value_heads // self.tp_size, num_slots,
+                               max_seq_len, block_size=block_size, num_blocks=num_blocks, device=device, dtype=dtype)
+        self.max_batch = max_batch or min(num_slots, 256) or 1
+        for i, layer in enumerate(self.model.layers):
+            attn = layer.self_attn
+            attn._kv_cache, attn._v_cache, attn._cache_seqlens = self.kv.k[i], self.kv.v[i], self.kv.seqlens
+        self.runtime = None
+
+    def _rt(self) -> Qwen3Runtime:
+        if self.runtime is None:
+            if self.kv is None:
+                raise RuntimeError("KV cache is not initialized")
+            if self._lm_shard is None:
+                raise RuntimeError("call fuse_qkv() before running the model")
+            cfg = self.config
+            dev = self.model.embed_tokens.weight.device
+            if self.rope is None or self.rope.device != dev:
+                self.rope = rope_table(cfg.max_position_embeddings, cfg.head_dim, cfg.rope_theta, dev)
+            layers = [LayerWeights(l.input_layernorm.weight.data, l.self_attn._qkv_proj.weight.data,
+                                   l.self_attn.q_norm.weight.data, l.self_attn.k_norm.weight.data,
+                                   l.self_attn.o_proj.weight.data, l.post_attention_layernorm.weight.data,
+                                   l.mlp._gate_up, l.mlp.down_proj.weight.data) for l in self.model.layers]
+            comm = TPComm(self.tp_rank, self.tp_size, get_tp_group())
+            self.runtime = Qwen3Runtime(
+                hidden=cfg.hidden_size, intermediate=cfg.intermediate_size, num_q_heads=cfg.num_attention_heads,
+                num_kv_heads=cfg.num_key_value_heads, vocab=cfg.vocab_size, eps=cfg.rms_norm_eps, layers=layers,
+                embed=self.model.embed_tokens.weight.data, final_norm=self.model.norm.weight.data,
+                lm_head=self._lm_shard, kv=self.kv, rope=self.rope, comm=comm,
+                vocab_offset=self.tp_rank * (cfg.vocab_size // self.tp_size), max_batch=self.max_batch,
+                use_graphs=self.use_cuda_graphs, prefill_chunk_tokens=self.prefill_chunk_tokens)
+        return self.runtime
+
+    def clear_slot(self, idx: int):
+        self.kv.release(int(idx))
+        self.kv.seqlens[int(idx)] = 0
+        self.kv.sync()
+
+    def clear_all_slots(self):
+        self.kv.clear_all()
+
+    @torch.inference_mode()
+    def forward(self, input_ids, position_ids, slot_indices=None):
+        """Same contract as the single-GPU model; every TP rank must call it.
+        Logits are gathered from the vocab shards, so every rank returns the
+        full [B, S, V] (the reference returns them on rank 0 only)."""
+        rt = self._rt()
+        B, S = input_ids.shape
+        if slot_indices is None or S != 1:
+            raise NotImplementedError("TP forward supports the decode step; prefill runs through LLMTP")
+        rows = [int(r) for r in slot_indices.tolist()]
+        rt.load_decode_inputs(input_ids[:, 0].tolist(), position_ids[:, 0].tolist(), rows)
+        shard = torch.empty((B, rt.vocab_local), dtype=torch.bfloat16, device=input_ids.device)
+        rt.decode_step(rows, logits=shard)
+        return tensor_model_parallel_all_gather(shard, dim=-1).unsqueeze(1)
+
+    # ------------------------------------------------------------------ weights
+    @classmethod
+    def from_state_dict(cls, state_dict: dict, config: Qwen3Config, device, dtype=torch.bfloat16):
+        """Build this rank's model from a full (CPU) state dict."""
+        with torch.device("meta"):
+            model = cls(config)
+        model = model.to_empty(device="cpu").to(dtype)
+        model = cls._convert_to_tp(model, {k: v.to(dtype) for k, v in state_dict.items()}, config)
+        return model.to(device)
+
+    @classmethod
+    def from_pretrained(cls, model_path: str, config: Qwen3Config, device, dtype):
+        """Every rank loads the full CPU state dict and slices it (model/model_tp.py:436-476)."""
+        from pathlib import Path
+
+        from safetensors import safe_open
+        f = Path(model_path) / "model.safetensors"
+        if not f.exists():
+            raise FileNotFoundError(f"No model.safetensors found in {model_path}")
+        sd = {}
+        with safe_open(str(f), framework="pt", device="cpu") as fh:
+            for key in fh.keys():
+                sd[key] = fh.get_tensor(key)
+        return cls.from_state_dict(sd, config, device, dtype)
+
+    @classmethod
+    def _convert_to_tp(cls, model, state_dict, config):
+        """Slice full weights for this rank (model/model_tp.py:478-567)."""
+        tp, rank = get_tp_world_size(), get_tp_rank()
+        model.model.embed_tokens.weight.data = state_dict["model.embed_tokens.weight"]
+        if not config.tie_word_embeddings and "lm_head.weight" in state_dict:
+            model.lm_head.weight.data = state_dict["lm_head.weight"]
+        for i in range(config.num_hidden_layers):
+            p = f"model.layers.{i}"
+            layer = model.model.layers[i]
+            layer.input_layernorm.weight.data = state_dict[f"{p}.input_layernorm.weight"]
+            layer.post_attention_layernorm.weight.data = state_dict[f"{p}.post_attention_layernorm.weight"]
+            qkv = torch.cat([state_dict[f"{p}.self_attn.q_proj.weight"], state_dict[f"{p}.self_attn.k_proj.weight"],
+                             state_dict[f"{p}.self_attn.v_proj.weight"]], 0)
+            (q0, q1), (k0, k1), (v0, v1) = qkv_rank_rows(config.num_attention_heads, config.num_key_value_heads,
+                                                          config.head_dim, rank, tp)
+            layer.self_attn._qkv_proj.weight.data = torch.cat([qkv[q0:q1], qkv[k0:k1], qkv[v0:v1]], 0)
+            layer.self_attn.q_norm.weight.data = state_dict[f"{p}.self_attn.q_norm.weight"]
+            layer.self_attn.k_norm.weight.data = state_dict[f"{p}.self_attn.k_norm.weight"]
+            layer.self_attn.o_proj.weight.data = split_tensor_along_dim(state_dict[f"{p}.self_attn.o_proj.weight"],
+                                                                        tp, dim=1)
+            layer.mlp.gate_proj.weight.data = split_tensor_along_dim(state_dict[f"{p}.mlp.gate_proj.weight"], tp, 0)
+            layer.mlp.up_proj.weight.data = split_tensor_along_dim(state_dict[f"{p}.mlp.up_proj.weight"], tp, 0)
+            layer.mlp.down_proj.weight.data = split_tensor_along_dim(state_dict[f"{p}.mlp.down_proj.weight"], tp, 1)
+        model.model.norm.weight.data = state_dict["model.norm.weight"]
+        return model
+
+    @classmethod
+    def random_init(cls, config: Qwen3Config, device, dtype=torch.bfloat16, seed: int = 0, std: float = 0.02):
+        """Per-rank random shards generated on the device (throughput runs;
+        the shards of different ranks are independent draws)."""
+        with torch.device("meta"):
+            model = cls(config)
+        model = model.to_empty(device=device).to(dtype)
+        g = torch.Generator(device=device).manual_seed(seed * 1009 + get_tp_rank())
+        with torch.no_grad():
+            for name, prm in model.named_parameters():
+                if name.endswith("norm.weight") or "layernorm" in name:
+                    prm.fill_(1.0)
+                else:
+                    prm.normal_(0.0, std, generator=g)
+        return model

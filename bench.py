@@ -62,8 +62,12 @@ def peaks():
 class ClockSampler:
     """nvidia-smi clock/throttle sampling during the timed region."""
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, device_index: int):
+        # nvidia-smi numbering can differ from CUDA's: address the GPU by UUID.
+        try:
+            self.index = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
+        except Exception:  # noqa: BLE001
+            self.index = str(device_index)
         self.proc = None
         self.lines = []
 
@@ -147,9 +151,10 @@ def build_engine(cfg2, device, use_graphs=True):
                use_cuda_graphs=use_graphs, device=device)
 
 
-def device_job(llm, prompts, out_tokens):
+def device_job(llm, prompts, out_tokens, mark=None):
     """One whole job on device: prefill all prompts, then out_tokens-1 decode
-    steps replaying the decode graph.  Returns nothing (tokens stay on device)."""
+    steps replaying the decode graph (tokens stay on device).  `mark`, a CUDA
+    event, is recorded between the prefill and the decode loop."""
     rt = llm.model._rt()
     kv = llm.model.kv
     rows = list(range(len(prompts)))
@@ -158,6 +163,8 @@ def device_job(llm, prompts, out_tokens):
     kv.sync()
     first = rt.prefill(prompts, rows)
     rt.buf.ids[:len(rows)].copy_(first)
+    if mark is not None:
+        mark.record(torch.cuda.current_stream())
     rt.load_positions_rows([len(p) for p in prompts], rows)
     for _ in range(out_tokens - 1):
         rt.decode_step(rows)
@@ -195,14 +202,16 @@ def run_cfg2(args, device):
     launches0 = lib.aacc_launch_count()
     graph_before = rt.graph_replays
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    elapsed = 0.0
+    em = torch.cuda.Event(enable_timing=True)
+    elapsed = prefill_s = 0.0
     with ClockSampler(torch.cuda.current_device()) as clk:
         for _ in range(args.steps):
             e0.record(stream)
-            rows = device_job(llm, prompts, cfg2.out)
+            rows = device_job(llm, prompts, cfg2.out, mark=em)
             e1.record(stream)
             e1.synchronize()
             elapsed += e0.elapsed_time(e1) / 1e3
+            prefill_s += e0.elapsed_time(em) / 1e3
             reset_job(llm, rows)
     torch.cuda.synchronize()
     _lib.raise_on_device_error("timed region")
@@ -212,6 +221,9 @@ def run_cfg2(args, device):
     t_max = max_over_ranks(args, elapsed)
     out_tok = cfg2.n_seqs * cfg2.out
     value = args.world * out_tok * args.steps / t_max
+    if args.profile:  # profiler capture: only the timed jobs run
+        return {"metric": "output tok/s", "value": round(value, 1), "unit": "output tok/s",
+                "note": "profiler run: not a bench value", "gpu_launches": int(lib.aacc_launch_count() - launches0)}
 
     # ---- roofline of the dominant kernel (paged decode attention) on the
     # end-of-job KV state: every row at prompt + out - 1 cached tokens.
@@ -250,9 +262,27 @@ def run_cfg2(args, device):
                    "parallelism": f"dp{args.world}" if args.world > 1 else "single",
                    "l2": "inputs larger than L2 (KV cache ~60 GB, weights 1.2 GB per step)"},
         "e2e": e2e, "roofline": roof, "gpu_launches": int(launches), "clocks": clk.summary(),
-        "decode_tok_per_s_device": None,
+        "phases": phase_summary(cfg2, args.steps, elapsed, prefill_s, llm.config),
     }
     return line
+
+
+def phase_summary(cfg2, steps, elapsed, prefill_s, cfg):
+    """Prefill / decode split of the timed jobs and the whole-job HBM roofline
+    (weights + KV bytes of every decode step over the measured copy bandwidth)."""
+    pk, kind = peaks()
+    decode_s = (elapsed - prefill_s) / steps
+    n_dec = cfg2.out - 1
+    kv_tok = 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * cfg.head_dim * 2
+    w_bytes = 1.192e9
+    ctx = cfg2.prompt + 1 + np.arange(n_dec)  # tokens attended at each decode step
+    dec_bytes = n_dec * w_bytes + cfg2.n_seqs * kv_tok * float(ctx.sum() + n_dec)
+    ideal = dec_bytes / (pk["hbm_gbs"] * 1e9)
+    return {"prefill_ms": round(prefill_s / steps * 1e3, 1), "decode_ms": round(decode_s * 1e3, 1),
+            "decode_ms_per_step": round(decode_s / n_dec * 1e3, 3),
+            "decode_tok_per_s": round(cfg2.n_seqs * n_dec / decode_s, 1),
+            "decode_hbm_bytes": dec_bytes, "decode_roofline_frac": round(ideal / decode_s, 3),
+            "peak_kind": kind}
 
 
 def attention_roofline(llm, rows, reps=20):
@@ -352,6 +382,55 @@ def run_attn(args, device):
             "gpu_launches": 2 * args.steps, "clocks": clk.summary()}
 
 
+# --------------------------------------------------------------------------- prefill GEMMs (tensor pipe)
+def run_gemm(args, device):
+    """The four cfg2 prefill projections on one prefill chunk (M tokens)."""
+    from awesome_acceleration_b200 import _lib, kernels as Kk
+    from awesome_acceleration_b200.runtime import interleave_gate_up
+    M = 8192 if args.small else 32768
+    H, I, hq, hkv = 1024, 3072, 16, 8
+    g = torch.Generator(device=device).manual_seed(3)
+    x = torch.randn((M, H), generator=g, device=device).to(torch.bfloat16)
+    a = torch.randn((M, I), generator=g, device=device).to(torch.bfloat16)
+    xo = torch.randn((M, hq * 128), generator=g, device=device).to(torch.bfloat16)
+    w = {n: (torch.randn(s, generator=g, device=device) * 0.02).to(torch.bfloat16) for n, s in
+         [("qkv", ((hq + 2 * hkv) * 128, H)), ("o", (H, hq * 128)), ("gu", (2 * I, H)), ("d", (H, I))]}
+    w["gu"] = interleave_gate_up(w["gu"][:I], w["gu"][I:]).contiguous()
+    ops = {"qkv_proj": (lambda: Kk.gemm(x, w["qkv"]), 2 * M * w["qkv"].shape[0] * H),
+           "o_proj": (lambda: Kk.gemm(xo, w["o"]), 2 * M * H * hq * 128),
+           "gate_up_silu": (lambda: Kk.gemm_silu_mul(x, w["gu"]), 2 * M * 2 * I * H),
+           "down_proj": (lambda: Kk.gemm(a, w["d"]), 2 * M * H * I)}
+    stream = torch.cuda.current_stream()
+    res = {}
+    pk, kind = peaks()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        for name, (fn, flops) in ops.items():
+            for _ in range(args.warmup):
+                fn()
+            ts = []
+            for _ in range(args.steps):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                fn()
+                e1.record(stream)
+                e1.synchronize()
+                ts.append(e0.elapsed_time(e1) / 1e3)
+            t = statistics.mean(ts)
+            res[name] = {"us": round(t * 1e6, 1), "tflops": round(flops / t / 1e12, 1),
+                         "frac": round(flops / t / 1e12 / pk["bf16_tflops"], 3)}
+    _lib.raise_on_device_error("gemm bench")
+    tot_f = sum(f for _, f in ops.values())
+    tot_t = sum(r["us"] for r in res.values()) / 1e6
+    ach = tot_f / tot_t / 1e12
+    return {"metric": f"prefill projection GEMMs TFLOP/s (M={M} tokens, Qwen3-0.6B shapes)", "value": round(ach, 1),
+            "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "cfg2 prefill GEMMs (one chunk)", "per_op": res},
+            "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": round(ach / pk["bf16_tflops"], 3), "traffic": None, "peak_kind": kind},
+            "gpu_launches": 4 * (args.steps + args.warmup), "clocks": clk.summary()}
+
+
 # --------------------------------------------------------------------------- CPU baseline (oracle)
 def cpu_sample(n_seqs=4, prompt=1024, out=8, seed=99):
     """The reference's CPU code path (restated by the oracle, bf16, all host
@@ -409,9 +488,11 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "attn"])
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "attn", "gemm"])
     ap.add_argument("--small", action="store_true", help="small case for profiler captures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="profiler capture: warm-up + timed jobs only (no roofline/e2e/CPU legs)")
     args = ap.parse_args()
     args.world = int(os.environ.get("WORLD_SIZE", "1"))
     args.rank = int(os.environ.get("RANK", "0"))
@@ -427,8 +508,8 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                              device_id=device)
     try:
-        line = run_attn(args, device) if args.workload == "attn" else run_cfg2(args, device)
-        if args.rank == 0 and args.workload == "cfg2" and not args.no_cpu_baseline:
+        line = {"attn": run_attn, "gemm": run_gemm, "cfg2": run_cfg2}[args.workload](args, device)
+        if args.rank == 0 and args.workload == "cfg2" and not (args.no_cpu_baseline or args.profile):
             v, info = cpu_sample()
             line["cpu_baseline"] = {"value": round(v, 3), "unit": "output tok/s", "cores": info["cores"],
                                     "kind": "port", "sample": info["sample"]}
