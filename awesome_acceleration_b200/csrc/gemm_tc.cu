@@ -26,11 +26,15 @@
 
 namespace aacc {
 
-enum Epi { EPI_STORE = 0, EPI_SILU = 1, EPI_QKV = 2, EPI_ARGMAX = 3 };
+enum Epi { EPI_STORE = 0, EPI_SILU = 1, EPI_QKV = 2, EPI_ARGMAX = 3, EPI_PARTIAL = 4 };
 
 struct EpiParams {
   bf16* out;
   int64_t ldo;
+  // EPI_PARTIAL (split-K): fp32 partial sums part[split][M][N]
+  float* part;
+  int64_t part_rows;  // M
+  int kb_per_split;   // 64-wide K slabs per split (grid.z splits); 0 = all
   // EPI_QKV
   const bf16* qn_w;
   const bf16* kn_w;
@@ -147,6 +151,26 @@ __device__ __forceinline__ void epilogue_group(uint32_t tcol, int64_t m, bool ro
         } else {
           for (int i = 0; i < 16; ++i)
             if (n0 + c + i < N) p.out[m * p.ldo + n0 + c + i] = tobf(v[i]);
+        }
+      }
+    }
+  } else if constexpr (EPI == EPI_PARTIAL) {
+    // fp32 partial of this K split; summed (in split order) by the consumer.
+    float* dst = p.part + ((int64_t)blockIdx.z * p.part_rows + m) * N + n0;
+#pragma unroll 1
+    for (int c = 0; c < 128; c += 16) {
+      float v[16];
+      tmem_ld16(tcol + c, v);
+      if (row_ok) {
+        if (n0 + c + 16 <= N) {
+          float4* d4 = reinterpret_cast<float4*>(dst + c);
+          d4[0] = make_float4(v[0], v[1], v[2], v[3]);
+          d4[1] = make_float4(v[4], v[5], v[6], v[7]);
+          d4[2] = make_float4(v[8], v[9], v[10], v[11]);
+          d4[3] = make_float4(v[12], v[13], v[14], v[15]);
+        } else {
+          for (int i = 0; i < 16; ++i)
+            if (n0 + c + i < N) dst[c + i] = v[i];
         }
       }
     }
@@ -288,7 +312,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t m0 = (int64_t)blockIdx.y * (128 * MT);
   const int64_t n_base = (int64_t)blockIdx.x * BN;
-  const int nk = K / 64;
+  // K slabs of this split: [kb0, kb0 + nk).
+  const int nk_all = K / 64;
+  const int kb0 = p.kb_per_split > 0 ? (int)blockIdx.z * p.kb_per_split : 0;
+  const int nk = p.kb_per_split > 0 ? min(p.kb_per_split, nk_all - kb0) : nk_all;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::STAGES; ++i) {
@@ -321,8 +348,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int st = kb % C::STAGES;
       if (kb >= C::STAGES && !mbar_wait(&empty[st], ((kb / C::STAGES) - 1) & 1, p.err, abort)) break;
       mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
-      tma_load_2d_hint(a_ring + st * C::A_BYTES, &tma, &full[st], kb * 64, (int)m0, pol_a);
-      tma_load_2d_hint(b_ring + st * C::B_BYTES, &tmb, &full[st], kb * 64, (int)n_base, pol_b);
+      tma_load_2d_hint(a_ring + st * C::A_BYTES, &tma, &full[st], (kb0 + kb) * 64, (int)m0, pol_a);
+      tma_load_2d_hint(b_ring + st * C::B_BYTES, &tmb, &full[st], (kb0 + kb) * 64, (int)n_base, pol_b);
       ++issued;
     }
     for (int st = 0; st < C::STAGES && st < issued; ++st) {
@@ -423,7 +450,7 @@ __global__ void argmax_merge_groups_kernel(const float* __restrict__ pv, const i
 // ---- host launch --------------------------------------------------------------
 template <int BN, int MT, int EPI>
 static int launch_gemm(const void* x, const void* w, int64_t M, int64_t N, int64_t K, const EpiParams& p,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, int splits = 1) {
   using C = GemmCfg<BN, MT>;
   CUtensorMap ta, tb;
   int st = make_tmap_2d(&ta, x, K, M, K * 2, 64, 128 * MT, true);
@@ -432,17 +459,21 @@ static int launch_gemm(const void* x, const void* w, int64_t M, int64_t N, int64
   if (st) return st;
   auto kern = gemm_tc_kernel<BN, MT, EPI>;
   set_smem_once<gemm_tc_kernel<BN, MT, EPI>>((int)C::SMEM);
-  dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + 128 * MT - 1) / (128 * MT)));
+  dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + 128 * MT - 1) / (128 * MT)), (unsigned)splits);
   kern<<<grid, kGemmThreads, C::SMEM, stream>>>(ta, tb, M, N, (int)K, p);
   return check_launch("gemm_tc_kernel");
 }
 
+// Tile shapes: decode batches (M <= 256) use 128x128 tiles, one CTA per
+// 128-row half of the batch, so twice the CTAs stream the weights (the second
+// read of a weight tile hits L2) and twice the SMs share the tensor work --
+// at M = 256 a weight byte feeds 256 FMAs, so the decode GEMMs need every
+// SM's tensor pipe as much as its bandwidth.  Prefill uses 256x256 tiles.
 template <int EPI>
 static int gemm_dispatch(const void* x, const void* w, int64_t M, int64_t N, int64_t K, const EpiParams& p,
-                         cudaStream_t stream) {
-  if (M <= 128) return launch_gemm<128, 1, EPI>(x, w, M, N, K, p, stream);
-  if (M <= 256) return launch_gemm<128, 2, EPI>(x, w, M, N, K, p, stream);
-  return launch_gemm<256, 2, EPI>(x, w, M, N, K, p, stream);
+                         cudaStream_t stream, int splits = 1) {
+  if (M <= 256) return launch_gemm<128, 1, EPI>(x, w, M, N, K, p, stream, splits);
+  return launch_gemm<256, 2, EPI>(x, w, M, N, K, p, stream, splits);
 }
 
 static int gemm_check(const void* x, const void* w, int64_t M, int64_t N, int64_t K, const char* what) {
@@ -470,6 +501,22 @@ int aacc_gemm(const void* x, const void* w, void* out, int64_t M, int64_t N, int
   p.ldo = N;
   p.err = device_error_ptr();
   return gemm_dispatch<EPI_STORE>(x, w, M, N, K, p, stream);
+}
+
+int aacc_gemm_splitk(const void* x, const void* w, float* partial, int64_t M, int64_t N, int64_t K, int splits,
+                     cudaStream_t stream) {
+  int st = gemm_check(x, w, M, N, K, "gemm_splitk");
+  if (st || M == 0) return st;
+  const int nk = (int)(K / 64);
+  if (splits < 1 || nk % splits)
+    return set_error(AACC_ERR_INVALID, "gemm_splitk: splits %d must divide K/64 = %d", splits, nk);
+  if (!aligned16(partial) || (N % 4)) return set_error(AACC_ERR_INVALID, "gemm_splitk: partial rows must be 16-byte aligned");
+  EpiParams p{};
+  p.part = partial;
+  p.part_rows = M;
+  p.kb_per_split = nk / splits;
+  p.err = device_error_ptr();
+  return gemm_dispatch<EPI_PARTIAL>(x, w, M, N, K, p, stream, splits);
 }
 
 int aacc_gemm_silu_mul(const void* x, const void* w_gate_up, void* out, int64_t M, int64_t I, int64_t K,

@@ -96,6 +96,58 @@ __global__ void __launch_bounds__(kNormMaxThreads)
   norm_row<V>(a, w, y + row * hidden, eps, hidden);
 }
 
+// Sum the split-K partials of 8 consecutive columns (split order, fp32).
+__device__ __forceinline__ void sum_partials8(const float* __restrict__ part, int S, int64_t split_stride, float (&d)[8]) {
+  float4 a = reinterpret_cast<const float4*>(part)[0], b = reinterpret_cast<const float4*>(part)[1];
+  d[0] = a.x; d[1] = a.y; d[2] = a.z; d[3] = a.w; d[4] = b.x; d[5] = b.y; d[6] = b.z; d[7] = b.w;
+  for (int s = 1; s < S; ++s) {
+    a = reinterpret_cast<const float4*>(part + s * split_stride)[0];
+    b = reinterpret_cast<const float4*>(part + s * split_stride)[1];
+    d[0] += a.x; d[1] += a.y; d[2] += a.z; d[3] += a.w; d[4] += b.x; d[5] += b.y; d[6] += b.z; d[7] += b.w;
+  }
+}
+
+template <int V>
+__global__ void __launch_bounds__(kNormMaxThreads)
+    splitk_add_rmsnorm_kernel(const float* __restrict__ part, int S, int64_t rows, bf16* __restrict__ residual,
+                              const bf16* __restrict__ w, bf16* __restrict__ y, int hidden, float eps) {
+  const int64_t row = blockIdx.x;
+  const int64_t stride = rows * hidden;
+  float a[V * 8];
+  load_row<V>(a, residual + row * hidden);
+#pragma unroll
+  for (int vv = 0; vv < V; ++vv) {
+    const int col = (vv * blockDim.x + threadIdx.x) * 8;
+    float d[8];
+    sum_partials8(part + row * hidden + col, S, stride, d);
+    uint4 ov;
+    uint32_t* ou = reinterpret_cast<uint32_t*>(&ov);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = vv * 8 + 2 * j;
+      a[i] = rbf(a[i] + rbf(d[2 * j]));
+      a[i + 1] = rbf(a[i + 1] + rbf(d[2 * j + 1]));
+      ou[j] = pack_bf16(a[i], a[i + 1]);
+    }
+    *reinterpret_cast<uint4*>(residual + row * hidden + col) = ov;
+  }
+  norm_row<V>(a, w, y + row * hidden, eps, hidden);
+}
+
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int S, int64_t n8, int64_t stride,
+                                     bf16* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  float d[8];
+  sum_partials8(part + i * 8, S, stride, d);
+  uint4 ov;
+  ov.x = pack_bf16(d[0], d[1]);
+  ov.y = pack_bf16(d[2], d[3]);
+  ov.z = pack_bf16(d[4], d[5]);
+  ov.w = pack_bf16(d[6], d[7]);
+  reinterpret_cast<uint4*>(out)[i] = ov;
+}
+
 template <int V>
 __global__ void __launch_bounds__(kNormMaxThreads)
     embed_rmsnorm_kernel(const int64_t* __restrict__ ids, const bf16* __restrict__ table, int64_t vocab,
@@ -163,6 +215,27 @@ int aacc_add_rmsnorm(const void* delta, void* residual, const void* w, void* y, 
   AACC_NORM_DISPATCH(add_rmsnorm_kernel, (const bf16*)delta, (bf16*)residual, (const bf16*)w, (bf16*)y, (int)hidden,
                      eps)
   return check_launch("add_rmsnorm");
+}
+
+int aacc_splitk_add_rmsnorm(const float* partial, int splits, void* residual, const void* w, void* y, int64_t rows,
+                            int64_t hidden, float eps, cudaStream_t stream) {
+  int threads, V;
+  int st = norm_shape(rows, hidden, "splitk_add_rmsnorm", &threads, &V);
+  if (st || rows == 0) return st;
+  if (splits < 1 || !aligned16(partial)) return set_error(AACC_ERR_INVALID, "splitk_add_rmsnorm: bad partials");
+  AACC_NORM_DISPATCH(splitk_add_rmsnorm_kernel, partial, splits, rows, (bf16*)residual, (const bf16*)w, (bf16*)y,
+                     (int)hidden, eps)
+  return check_launch("splitk_add_rmsnorm");
+}
+
+int aacc_splitk_reduce(const float* partial, int splits, void* out, int64_t rows, int64_t cols, cudaStream_t stream) {
+  if (rows < 0 || cols <= 0 || cols % 8 || splits < 1 || !aligned16(partial) || !aligned16(out))
+    return set_error(AACC_ERR_INVALID, "splitk_reduce: cols must be a multiple of 8, pointers 16-byte aligned");
+  if (rows == 0) return AACC_OK;
+  const int64_t n8 = rows * cols / 8;
+  splitk_reduce_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, stream>>>(partial, splits, n8, rows * cols,
+                                                                         (bf16*)out);
+  return check_launch("splitk_reduce");
 }
 
 int aacc_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, void* residual, const void* w, void* y,

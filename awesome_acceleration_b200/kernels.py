@@ -135,6 +135,40 @@ def gemm(x, w, out=None):
     return out
 
 
+def pick_splits(M: int, N: int, K: int, sms: int = 148, cap: int = 16) -> int:
+    """Largest divisor of K/64 (at most `cap`) that keeps the split-K grid
+    within one wave of CTAs."""
+    tiles = ((N + 127) // 128) * ((M + 127) // 128)
+    nk = K // 64
+    best = 1
+    for d in range(1, min(nk, cap) + 1):
+        if nk % d == 0 and tiles * d <= sms:
+            best = d
+    return best
+
+
+def gemm_splitk(x, w, partial, splits: int):
+    """partial [splits, M, N] fp32 <- split-K partial products of x @ w^T."""
+    M, K = x.shape
+    N = w.shape[0]
+    _lib.check(_lib_().aacc_gemm_splitk(_p(x), _p(w), _p(partial), M, N, K, splits, _stream()), "gemm_splitk")
+    return partial
+
+
+def splitk_add_rmsnorm(partial, splits: int, residual, w, eps: float, out):
+    H = residual.shape[-1]
+    rows = residual.numel() // H
+    _lib.check(_lib_().aacc_splitk_add_rmsnorm(_p(partial), splits, _p(residual), _p(w), _p(out), rows, H, eps,
+                                               _stream()), "splitk_add_rmsnorm")
+    return out
+
+
+def splitk_reduce(partial, splits: int, out):
+    rows, cols = out.shape
+    _lib.check(_lib_().aacc_splitk_reduce(_p(partial), splits, _p(out), rows, cols, _stream()), "splitk_reduce")
+    return out
+
+
 def gemm_silu_mul(x, w_gate_up, out=None):
     M, K = x.shape
     I = w_gate_up.shape[0] // 2

@@ -88,7 +88,8 @@ class TPComm:
             torch.distributed.all_reduce(t, group=self.group)
 
     def all_gather(self, out: torch.Tensor, t: torch.Tensor) -> None:
-        torch.distributed.all_gather_into_tensor(out, t, group=self.group)
+        """out [size, n] <- every rank's t [n] (rank order)."""
+        torch.distributed.all_gather_into_tensor(out.view(-1), t, group=self.group)
 
 
 class _DecodeBuffers:
@@ -109,6 +110,8 @@ class _DecodeBuffers:
         self.lm_ws = torch.empty(K.lm_head_workspace_bytes(B, vocab), dtype=torch.uint8, device=device)
         self.best = torch.zeros(B, dtype=torch.float32, device=device)
         self.tok = torch.zeros(B, **i64)
+        # split-K partials of the RowParallel projections: at most 16 splits of [B, H] fp32
+        self.part = torch.empty(16 * B * H, dtype=torch.float32, device=device)
         if tp > 1:
             self.g_best = torch.zeros((tp, B), dtype=torch.float32, device=device)
             self.g_tok = torch.zeros((tp, B), **i64)
@@ -147,23 +150,38 @@ class Qwen3Runtime:
         self._tok_host = torch.zeros(max_batch, dtype=torch.int64).pin_memory()
 
     # ------------------------------------------------------------------ layers
-    def _layer_chain(self, x, res, delta, q, attn, act, attend, positions, slot_map):
+    def _row_parallel(self, inp, w, delta, res, norm_w, x, part):
+        """RowParallel projection + residual add + next RMSNorm.  Decode-sized
+        batches use split-K (every SM streams a K slice of the weight) and sum
+        the fp32 partials inside the norm kernel; under TP the bf16 partial
+        output is all-reduced first (RowParallelLinear, parallel_layers.py:190-195)."""
+        M = inp.shape[0]
+        splits = K.pick_splits(M, w.shape[0], w.shape[1]) if part is not None else 1
+        if splits > 1:
+            pv = part[:splits * M * w.shape[0]].view(splits, M, w.shape[0])
+            K.gemm_splitk(inp, w, pv, splits)
+            if self.comm.size == 1:
+                K.splitk_add_rmsnorm(pv, splits, res, norm_w, self.eps, out=x)
+                return
+            K.splitk_reduce(pv, splits, delta)
+        else:
+            K.gemm(inp, w, out=delta)
+        self.comm.all_reduce(delta)
+        K.add_rmsnorm(delta, res, norm_w, self.eps, out=x)
+
+    def _layer_chain(self, x, res, delta, q, attn, act, attend, positions, slot_map, part=None):
         """All layers for rows already embedded into (res, x); `attend(i, q, out)`
-        runs this layer's attention."""
+        runs this layer's attention; `part` (fp32 workspace) enables split-K."""
         L = len(self.layers)
         kv = self.kv
         for i, lw in enumerate(self.layers):
             K.qkv_norm_rope_store(x, lw.wqkv, lw.q_norm, lw.k_norm, self.eps, positions, self.rope, slot_map,
                                   kv.k[i], kv.v[i], self.Hq, q_out=q)
             attend(i, q, attn)
-            K.gemm(attn.view(attn.shape[0], -1), lw.wo, out=delta)
-            self.comm.all_reduce(delta)
-            K.add_rmsnorm(delta, res, lw.post_ln, self.eps, out=x)
+            self._row_parallel(attn.view(attn.shape[0], -1), lw.wo, delta, res, lw.post_ln, x, part)
             K.gemm_silu_mul(x, lw.w_gate_up, out=act)
-            K.gemm(act, lw.wd, out=delta)
-            self.comm.all_reduce(delta)
             nxt = self.layers[i + 1].in_ln if i + 1 < L else self.final_norm
-            K.add_rmsnorm(delta, res, nxt, self.eps, out=x)
+            self._row_parallel(act, lw.wd, delta, res, nxt, x, part)
 
     def _argmax(self, x, tokens, best, ws, logits=None, g_best=None, g_tok=None):
         """Greedy token of each row of x; under TP every rank scores its vocab
@@ -187,7 +205,7 @@ class Qwen3Runtime:
                                      scale=self.scale, max_context=self.max_context, workspace=b.attn_ws, out=out)
 
         self._layer_chain(b.x[:B], b.res[:B], b.delta[:B], b.q[:B], b.attn[:B], b.act[:B], attend, pos,
-                          b.slot_map[:B])
+                          b.slot_map[:B], part=b.part)
         g_best = b.g_best[:, :B] if self.comm.size > 1 else None
         g_tok = b.g_tok[:, :B] if self.comm.size > 1 else None
         self._argmax(b.x[:B], ids, b.best[:B], b.lm_ws, logits=logits, g_best=g_best, g_tok=g_tok)

@@ -384,10 +384,14 @@ def run_attn(args, device):
 
 # --------------------------------------------------------------------------- prefill GEMMs (tensor pipe)
 def run_gemm(args, device):
-    """The four cfg2 prefill projections on one prefill chunk (M tokens)."""
+    """The four cfg2 projections on one prefill chunk (M tokens) or, with
+    --decode, on one decode batch (M = 256 rows; weight-bandwidth bound)."""
     from awesome_acceleration_b200 import _lib, kernels as Kk
     from awesome_acceleration_b200.runtime import interleave_gate_up
-    M = 8192 if args.small else 32768
+    if args.decode:
+        M = 32 if args.small else 256
+    else:
+        M = 8192 if args.small else 32768
     H, I, hq, hkv = 1024, 3072, 16, 8
     g = torch.Generator(device=device).manual_seed(3)
     x = torch.randn((M, H), generator=g, device=device).to(torch.bfloat16)
@@ -416,8 +420,10 @@ def run_gemm(args, device):
                 e1.synchronize()
                 ts.append(e0.elapsed_time(e1) / 1e3)
             t = statistics.mean(ts)
+            wbytes = flops // (2 * M) * 2  # weight bytes: N*K bf16
             res[name] = {"us": round(t * 1e6, 1), "tflops": round(flops / t / 1e12, 1),
-                         "frac": round(flops / t / 1e12 / pk["bf16_tflops"], 3)}
+                         "frac": round(flops / t / 1e12 / pk["bf16_tflops"], 3),
+                         "weight_gbs": round(wbytes / t / 1e9, 1)}
     _lib.raise_on_device_error("gemm bench")
     tot_f = sum(f for _, f in ops.values())
     tot_t = sum(r["us"] for r in res.values()) / 1e6
@@ -491,6 +497,7 @@ def main():
     ap.add_argument("--workload", default="cfg2", choices=["cfg2", "attn", "gemm"])
     ap.add_argument("--small", action="store_true", help="small case for profiler captures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode", action="store_true", help="gemm workload: decode-batch shapes")
     ap.add_argument("--profile", action="store_true",
                     help="profiler capture: warm-up + timed jobs only (no roofline/e2e/CPU legs)")
     args = ap.parse_args()

@@ -124,6 +124,18 @@ int aacc_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t hi
 int aacc_add_rmsnorm(const void* delta, void* residual, const void* w, void* y, int64_t rows,
                      int64_t hidden, float eps, cudaStream_t stream);
 
+/* delta = bf16(sum_s partial[s]) (split order), then as aacc_add_rmsnorm:
+ * residual = bf16(residual + delta); y = rmsnorm(residual).  The split-K
+ * o_proj / down_proj output feeding the residual add and the next norm
+ * (model/model.py:258-263, :190 + :265). */
+int aacc_splitk_add_rmsnorm(const float* partial, int splits, void* residual, const void* w, void* y,
+                            int64_t rows, int64_t hidden, float eps, cudaStream_t stream);
+
+/* out = bf16(sum_s partial[s]) for partial [splits][rows][cols] (TP: the
+ * bf16 RowParallel output that the all-reduce then sums). */
+int aacc_splitk_reduce(const float* partial, int splits, void* out, int64_t rows, int64_t cols,
+                       cudaStream_t stream);
+
 /* residual = table[ids]; y = rmsnorm(residual).  embed_tokens + first
  * input_layernorm (model/model.py:280, :213). */
 int aacc_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, void* residual,
@@ -138,6 +150,14 @@ int aacc_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, voi
  * down_proj :190, RowParallelLinear parallel_layers.py:190). */
 int aacc_gemm(const void* x, const void* w, void* out, int64_t M, int64_t N, int64_t K,
               cudaStream_t stream);
+
+/* Split-K GEMM: partial[s][M][N] (fp32) = x[:, Ks] @ w[:, Ks]^T for the s-th
+ * of `splits` equal K ranges (splits must divide K/64).  Spreads a small
+ * decode GEMM (N = hidden, e.g. o_proj / down_proj) over every SM; the
+ * partials are summed in split order by aacc_splitk_add_rmsnorm or
+ * aacc_splitk_reduce.  Same reference call sites as aacc_gemm. */
+int aacc_gemm_splitk(const void* x, const void* w, float* partial, int64_t M, int64_t N, int64_t K, int splits,
+                     cudaStream_t stream);
 
 /* out[M][I] = bf16(silu(bf16(x@Wg^T))) * bf16(x@Wu^T), rounded per op as the
  * eager reference.  w_gate_up rows interleave gate/up in groups of 64:

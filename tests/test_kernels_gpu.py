@@ -238,6 +238,35 @@ def test_gemm(cuda, M, N, Kd):
     assert err <= tol, f"max-abs {err} > {tol}"
 
 
+@pytest.mark.parametrize("M,N,Kd", [(1, 1024, 2048), (32, 1024, 3072), (200, 1024, 2048), (256, 512, 512)])
+def test_splitk_gemm_add_rmsnorm(cuda, M, N, Kd):
+    """Split-K partials summed by splitk_reduce / splitk_add_rmsnorm equal the
+    unsplit GEMM followed by add_rmsnorm (up to fp32 summation order)."""
+    g = torch.Generator().manual_seed(M + N + Kd)
+    x = torch.randn((M, Kd), generator=g).to(BF).to(cuda)
+    w = (torch.randn((N, Kd), generator=g) * 0.02).to(BF).to(cuda)
+    res0 = torch.randn((M, N), generator=g).to(BF).to(cuda)
+    nw = (1 + 0.1 * torch.randn(N, generator=g)).to(BF).to(cuda)
+    splits = K().pick_splits(M, N, Kd)
+    assert splits > 1
+    part = torch.empty((splits, M, N), dtype=torch.float32, device=cuda)
+    K().gemm_splitk(x, w, part, splits)
+    ref_f32 = x.float() @ w.float().t()
+    assert (part.sum(0) - ref_f32).abs().max().item() <= 1e-3 * ref_f32.abs().max().item() + 1e-4
+    delta = torch.empty((M, N), dtype=BF, device=cuda)
+    K().splitk_reduce(part, splits, delta)
+    acc = part[0].clone()
+    for s in range(1, splits):  # the kernels sum the partials in split order
+        acc += part[s]
+    assert torch.equal(delta, acc.to(BF))
+    res = res0.clone()
+    y = torch.empty_like(res)
+    K().splitk_add_rmsnorm(part, splits, res, nw, 1e-6, out=y)
+    res_ref = res0.clone()
+    y_ref = K().add_rmsnorm(delta, res_ref, nw, 1e-6)
+    assert torch.equal(res, res_ref) and torch.equal(y, y_ref)
+
+
 @pytest.mark.parametrize("M", [3, 256, 700])
 def test_gemm_silu_mul(cuda, M):
     from awesome_acceleration_b200.runtime import interleave_gate_up

@@ -1,0 +1,181 @@
+"""Multi-rank host logic of the TP path on CPU ranks (Gloo): process-group
+layout, weight sharding of the parallel layers, the RowParallel all-reduce
+placement, vocab-parallel argmax candidates, the leader/worker control
+protocol and failure propagation.  No GPU: the GEMM is replaced by a CPU
+matmul inside the test processes only."""
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _run(rank, world, port, fn, q, *args):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    try:
+        fn(rank, world, *args)
+        q.put((rank, None))
+    except BaseException:  # noqa: BLE001
+        q.put((rank, traceback.format_exc()))
+    finally:
+        import torch.distributed as dist
+        if dist.is_initialized():
+            try:
+                dist.destroy_process_group()
+            except Exception:  # noqa: BLE001
+                pass
+
+
+def spawn(world, fn, *args, timeout=120):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_run, args=(r, world, port, fn, q) + args) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        r, err = q.get(timeout=timeout)
+        results[r] = err
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    return results
+
+
+# ---------------------------------------------------------------------------- workers
+def _groups(rank, world, tp):
+    from awesome_acceleration_b200.model import distributed as D
+    D.init_distributed(tp, backend="gloo", timeout_s=30)
+    assert D.get_tp_world_size() == tp and D.get_dp_world_size() == world // tp
+    assert D.get_tp_rank() == rank % tp and D.get_dp_rank() == rank // tp
+    assert D.get_tp_leader_global_rank() == (rank // tp) * tp
+    assert D.is_tp_leader() == (rank % tp == 0) and D.is_global_rank_0() == (rank == 0)
+    # The TP group sums over consecutive ranks, the DP group over strided ranks.
+    import torch.distributed as dist
+    t = torch.tensor([float(rank)])
+    dist.all_reduce(t, group=D.get_tp_group())
+    base = (rank // tp) * tp
+    assert t.item() == sum(range(base, base + tp))
+    t = torch.tensor([float(rank)])
+    dist.all_reduce(t, group=D.get_dp_group())
+    assert t.item() == sum(range(rank % tp, world, tp))
+    obj = D.broadcast_object({"leader": rank} if D.is_tp_leader() else None, src=0)
+    assert obj == {"leader": base}
+
+
+def _layers(rank, world):
+    from awesome_acceleration_b200 import kernels
+    from awesome_acceleration_b200.model import distributed as D
+    from awesome_acceleration_b200.model import parallel_layers as PL
+    D.init_distributed(world, backend="gloo", timeout_s=30)
+    kernels.gemm = lambda x, w, out=None: (x.float() @ w.float().t()).to(x.dtype)  # CPU stand-in (test only)
+    g = torch.Generator().manual_seed(0)
+    H, I, Hq, Hkv, Dh = 64, 96, 4, 2, 16
+    lin = torch.nn.Linear(H, I, bias=False)
+    lin.weight.data = torch.randn((I, H), generator=g)
+    col = PL.ColumnParallelLinear.from_linear(lin)
+    assert col.weight.shape == (I // world, H)
+    assert torch.equal(col.weight, lin.weight[rank * I // world:(rank + 1) * I // world])
+    down = torch.nn.Linear(I, H, bias=False)
+    down.weight.data = torch.randn((H, I), generator=g)
+    row = PL.RowParallelLinear.from_linear(down)
+    assert row.weight.shape == (H, I // world)
+    x = torch.randn((3, 5, I), generator=g)
+    xs = x[..., rank * I // world:(rank + 1) * I // world].contiguous()
+    y = row(xs)  # partial matmul + all-reduce over the TP group
+    assert torch.allclose(y, x @ down.weight.t(), atol=1e-4)
+    full = torch.randn(((Hq + 2 * Hkv) * Dh, H), generator=g)
+    qkv = PL.QKVParallelLinear.from_fused_qkv(full, None, H, Hq, Hkv, Dh)
+    qr, kr = Hq // world * Dh, Hkv // world * Dh
+    exp = torch.cat([full[rank * qr:(rank + 1) * qr], full[Hq * Dh + rank * kr:Hq * Dh + (rank + 1) * kr],
+                     full[(Hq + Hkv) * Dh + rank * kr:(Hq + Hkv) * Dh + (rank + 1) * kr]])
+    assert torch.equal(qkv.weight, exp)
+    q, k, v = qkv(torch.randn((7, H), generator=g))
+    assert q.shape == (7, Hq // world, Dh) and k.shape == v.shape == (7, Hkv // world, Dh)
+    q, k, v = qkv(torch.randn((2, 3, H), generator=g))
+    assert q.shape == (2, 3, Hq // world, Dh)
+    with pytest.raises(ValueError):
+        qkv(torch.randn(H))
+
+
+def _vocab_argmax(rank, world):
+    """Every rank scores its vocab shard; gathering (max, id) candidates and
+    taking the highest value (lowest id on ties) equals the global argmax."""
+    import torch.distributed as dist
+    from awesome_acceleration_b200.model import distributed as D
+    D.init_distributed(world, backend="gloo", timeout_s=30)
+    g = torch.Generator().manual_seed(1)
+    B, V = 6, 40
+    logits = torch.randint(-3, 4, (B, V), generator=g).float()  # many ties
+    shard = V // world
+    local = logits[:, rank * shard:(rank + 1) * shard]
+    val, idx = local.max(-1)  # torch.max returns the first index of the max
+    idx = idx + rank * shard
+    gv = torch.empty((world, B))
+    gi = torch.empty((world, B), dtype=torch.int64)
+    dist.all_gather_into_tensor(gv.view(-1), val)
+    dist.all_gather_into_tensor(gi.view(-1), idx)
+    best = gv.max(0).values
+    cand = torch.where(gv == best, gi, torch.full_like(gi, 1 << 40))
+    assert torch.equal(cand.min(0).values, logits.argmax(-1))
+
+
+def _exit_propagates(rank, world):
+    """A worker that dies between steps turns the leader's next control
+    broadcast into an error within the process-group timeout (no hang)."""
+    import time
+    from awesome_acceleration_b200.model import distributed as D
+    D.init_distributed(world, backend="gloo", timeout_s=5)
+    if rank == 1:
+        os._exit(0)  # dies without joining the next collective
+    time.sleep(0.5)
+    t0 = time.time()
+    with pytest.raises(Exception):
+        D.broadcast_object({"action": "decode", "batch_size": 1}, src=0)
+        D.broadcast_object({"action": "decode", "batch_size": 1}, src=0)
+    assert time.time() - t0 < 60
+
+
+# ---------------------------------------------------------------------------- tests
+@pytest.mark.parametrize("world,tp", [(2, 2), (4, 2), (4, 4)])
+def test_process_groups(world, tp):
+    res = spawn(world, _groups, tp)
+    assert all(v is None for v in res.values()), res
+
+
+def test_parallel_layer_sharding_and_row_allreduce():
+    res = spawn(2, _layers)
+    assert all(v is None for v in res.values()), res
+
+
+def test_vocab_parallel_argmax_candidates():
+    res = spawn(2, _vocab_argmax)
+    assert all(v is None for v in res.values()), res
+
+
+def test_dead_worker_raises_instead_of_hanging():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_run, args=(r, 2, port, _exit_propagates, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    r, err = q.get(timeout=120)
+    assert r == 0 and err is None, err
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
