@@ -469,10 +469,15 @@ static int launch_gemm(const void* x, const void* w, int64_t M, int64_t N, int64
 // read of a weight tile hits L2) and twice the SMs share the tensor work --
 // at M = 256 a weight byte feeds 256 FMAs, so the decode GEMMs need every
 // SM's tensor pipe as much as its bandwidth.  Prefill uses 256x256 tiles.
+//
+// The lm_head (EPI_ARGMAX, N = vocab: thousands of tiles) is the exception:
+// there every SM is busy anyway and the per-SM shared-memory fill (TMA
+// throughput) is the limit, so 256x256 tiles, which re-read the activations
+// half as often and the weights once, are faster from M = 129 up.
 template <int EPI>
 static int gemm_dispatch(const void* x, const void* w, int64_t M, int64_t N, int64_t K, const EpiParams& p,
                          cudaStream_t stream, int splits = 1) {
-  if (M <= 256) return launch_gemm<128, 1, EPI>(x, w, M, N, K, p, stream, splits);
+  if (M <= 128 || (M <= 256 && EPI != EPI_ARGMAX)) return launch_gemm<128, 1, EPI>(x, w, M, N, K, p, stream, splits);
   return launch_gemm<256, 2, EPI>(x, w, M, N, K, p, stream, splits);
 }
 

@@ -135,14 +135,15 @@ def gemm(x, w, out=None):
     return out
 
 
-def pick_splits(M: int, N: int, K: int, sms: int = 148, cap: int = 16) -> int:
-    """Largest divisor of K/64 (at most `cap`) that keeps the split-K grid
-    within one wave of CTAs."""
+def pick_splits(M: int, N: int, K: int, sms: int = 148, cap: int = 16, max_elems: int | None = None) -> int:
+    """Largest divisor of K/64 (at most `cap`, and with splits*M*N fp32
+    partials fitting `max_elems`) that keeps the split-K grid within one wave
+    of CTAs (one 128x128 tile per SM)."""
     tiles = ((N + 127) // 128) * ((M + 127) // 128)
     nk = K // 64
     best = 1
     for d in range(1, min(nk, cap) + 1):
-        if nk % d == 0 and tiles * d <= sms:
+        if nk % d == 0 and tiles * d <= sms and (max_elems is None or d * M * N <= max_elems):
             best = d
     return best
 
@@ -160,6 +161,23 @@ def splitk_add_rmsnorm(partial, splits: int, residual, w, eps: float, out):
     rows = residual.numel() // H
     _lib.check(_lib_().aacc_splitk_add_rmsnorm(_p(partial), splits, _p(residual), _p(w), _p(out), rows, H, eps,
                                                _stream()), "splitk_add_rmsnorm")
+    return out
+
+
+def splitk_qkv_norm_rope_store(partial, splits: int, q_norm_w, k_norm_w, eps: float, positions, rope_cos_sin,
+                               slot_mapping, k_cache, v_cache, num_q_heads: int, q_out):
+    M = q_out.shape[0]
+    nb, hkv, bs, _ = k_cache.shape
+    _lib.check(_lib_().aacc_splitk_qkv_norm_rope_store(
+        _p(partial), splits, _p(q_norm_w), _p(k_norm_w), eps, _p(positions), _p(rope_cos_sin),
+        rope_cos_sin.shape[0], _p(slot_mapping), _p(q_out), _p(k_cache), _p(v_cache), nb, num_q_heads, hkv, bs, M,
+        _stream()), "splitk_qkv_norm_rope_store")
+    return q_out
+
+
+def splitk_silu_mul(partial, splits: int, out):
+    M, I = out.shape
+    _lib.check(_lib_().aacc_splitk_silu_mul(_p(partial), splits, _p(out), M, I, _stream()), "splitk_silu_mul")
     return out
 
 

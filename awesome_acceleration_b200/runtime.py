@@ -110,11 +110,12 @@ class _DecodeBuffers:
         self.lm_ws = torch.empty(K.lm_head_workspace_bytes(B, vocab), dtype=torch.uint8, device=device)
         self.best = torch.zeros(B, dtype=torch.float32, device=device)
         self.tok = torch.zeros(B, **i64)
-        # split-K partials of the RowParallel projections: at most 16 splits of [B, H] fp32
-        self.part = torch.empty(16 * B * H, dtype=torch.float32, device=device)
-        if tp > 1:
-            self.g_best = torch.zeros((tp, B), dtype=torch.float32, device=device)
-            self.g_tok = torch.zeros((tp, B), **i64)
+        # split-K fp32 partials of the decode projections (the split count is
+        # capped so that splits * B * N fits): 32 MB
+        self.part = torch.empty(max(8 << 20, 16 * B * H), dtype=torch.float32, device=device)
+        if tp > 1:  # all-gathered argmax candidates, viewed as [tp, batch] per step
+            self.g_best = torch.zeros(tp * B, dtype=torch.float32, device=device)
+            self.g_tok = torch.zeros(tp * B, **i64)
 
 
 class Qwen3Runtime:
@@ -150,13 +151,45 @@ class Qwen3Runtime:
         self._tok_host = torch.zeros(max_batch, dtype=torch.int64).pin_memory()
 
     # ------------------------------------------------------------------ layers
+    def _splits(self, M, w, part):
+        if part is None:
+            return 1
+        return K.pick_splits(M, w.shape[0], w.shape[1], max_elems=part.numel())
+
+    def _qkv(self, i, lw, x, positions, slot_map, q, part):
+        """Fused QKV projection + q/k-norm + RoPE + KV store (model/model.py:219-226)."""
+        kv = self.kv
+        M = x.shape[0]
+        splits = self._splits(M, lw.wqkv, part)
+        if splits > 1:
+            N = lw.wqkv.shape[0]
+            pv = part[:splits * M * N].view(splits, M, N)
+            K.gemm_splitk(x, lw.wqkv, pv, splits)
+            K.splitk_qkv_norm_rope_store(pv, splits, lw.q_norm, lw.k_norm, self.eps, positions, self.rope, slot_map,
+                                         kv.k[i], kv.v[i], self.Hq, q_out=q)
+        else:
+            K.qkv_norm_rope_store(x, lw.wqkv, lw.q_norm, lw.k_norm, self.eps, positions, self.rope, slot_map,
+                                  kv.k[i], kv.v[i], self.Hq, q_out=q)
+
+    def _gate_up(self, lw, x, act, part):
+        """gate/up projection + SiLU-mul (model/model.py:189-190)."""
+        M = x.shape[0]
+        splits = self._splits(M, lw.w_gate_up, part)
+        if splits > 1:
+            N = lw.w_gate_up.shape[0]
+            pv = part[:splits * M * N].view(splits, M, N)
+            K.gemm_splitk(x, lw.w_gate_up, pv, splits)
+            K.splitk_silu_mul(pv, splits, act)
+        else:
+            K.gemm_silu_mul(x, lw.w_gate_up, out=act)
+
     def _row_parallel(self, inp, w, delta, res, norm_w, x, part):
         """RowParallel projection + residual add + next RMSNorm.  Decode-sized
         batches use split-K (every SM streams a K slice of the weight) and sum
         the fp32 partials inside the norm kernel; under TP the bf16 partial
         output is all-reduced first (RowParallelLinear, parallel_layers.py:190-195)."""
         M = inp.shape[0]
-        splits = K.pick_splits(M, w.shape[0], w.shape[1]) if part is not None else 1
+        splits = self._splits(M, w, part)
         if splits > 1:
             pv = part[:splits * M * w.shape[0]].view(splits, M, w.shape[0])
             K.gemm_splitk(inp, w, pv, splits)
@@ -173,13 +206,11 @@ class Qwen3Runtime:
         """All layers for rows already embedded into (res, x); `attend(i, q, out)`
         runs this layer's attention; `part` (fp32 workspace) enables split-K."""
         L = len(self.layers)
-        kv = self.kv
         for i, lw in enumerate(self.layers):
-            K.qkv_norm_rope_store(x, lw.wqkv, lw.q_norm, lw.k_norm, self.eps, positions, self.rope, slot_map,
-                                  kv.k[i], kv.v[i], self.Hq, q_out=q)
+            self._qkv(i, lw, x, positions, slot_map, q, part)
             attend(i, q, attn)
             self._row_parallel(attn.view(attn.shape[0], -1), lw.wo, delta, res, lw.post_ln, x, part)
-            K.gemm_silu_mul(x, lw.w_gate_up, out=act)
+            self._gate_up(lw, x, act, part)
             nxt = self.layers[i + 1].in_ln if i + 1 < L else self.final_norm
             self._row_parallel(act, lw.wd, delta, res, nxt, x, part)
 
@@ -206,8 +237,9 @@ class Qwen3Runtime:
 
         self._layer_chain(b.x[:B], b.res[:B], b.delta[:B], b.q[:B], b.attn[:B], b.act[:B], attend, pos,
                           b.slot_map[:B], part=b.part)
-        g_best = b.g_best[:, :B] if self.comm.size > 1 else None
-        g_tok = b.g_tok[:, :B] if self.comm.size > 1 else None
+        t = self.comm.size
+        g_best = b.g_best[:t * B].view(t, B) if t > 1 else None
+        g_tok = b.g_tok[:t * B].view(t, B) if t > 1 else None
         self._argmax(b.x[:B], ids, b.best[:B], b.lm_ws, logits=logits, g_best=g_best, g_tok=g_tok)
         K.advance_seqlens(rows, kv.seqlens, pos)
 

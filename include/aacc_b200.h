@@ -180,6 +180,24 @@ int aacc_qkv_norm_rope_store(const void* x, const void* w_qkv, const void* q_nor
                              int num_q_heads, int num_kv_heads, int block_size, int64_t M,
                              int64_t K, cudaStream_t stream);
 
+/* The QKV epilogue of aacc_qkv_norm_rope_store applied to split-K partials
+ * partial [splits][M][(Hq+2Hkv)*128] (from aacc_gemm_splitk): sum in split
+ * order, q/k RMSNorm, RoPE, Q to q_out, K/V into the paged cache.  Lets the
+ * decode QKV projection use every SM.  Same reference lines as
+ * aacc_qkv_norm_rope_store. */
+int aacc_splitk_qkv_norm_rope_store(const float* partial, int splits, const void* q_norm_w,
+                                    const void* k_norm_w, float eps, const int64_t* positions,
+                                    const void* rope_cos_sin, int64_t max_pos, const int64_t* slot_mapping,
+                                    void* q_out, void* k_cache, void* v_cache, int64_t num_blocks,
+                                    int num_q_heads, int num_kv_heads, int block_size, int64_t M,
+                                    cudaStream_t stream);
+
+/* The SiLU-mul epilogue of aacc_gemm_silu_mul applied to split-K partials
+ * partial [splits][M][2I] of the interleaved gate/up GEMM -> out [M][I]
+ * (MLP.forward, model/model.py:189-190). */
+int aacc_splitk_silu_mul(const float* partial, int splits, void* out, int64_t M, int64_t I,
+                         cudaStream_t stream);
+
 /* Workspace bytes for aacc_lm_head_argmax. */
 int64_t aacc_lm_head_workspace_bytes(int64_t M, int64_t vocab);
 

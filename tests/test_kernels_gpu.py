@@ -267,6 +267,45 @@ def test_splitk_gemm_add_rmsnorm(cuda, M, N, Kd):
     assert torch.equal(res, res_ref) and torch.equal(y, y_ref)
 
 
+@pytest.mark.parametrize("M", [1, 32, 256])
+def test_splitk_qkv_and_silu_epilogues(cuda, M):
+    """Split-K QKV / SiLU epilogues agree with the fused single-pass GEMM
+    epilogues (same rounding points; only the fp32 summation order differs)."""
+    from awesome_acceleration_b200.runtime import interleave_gate_up, rope_table
+    g = torch.Generator().manual_seed(100 + M)
+    H, I, hq, hkv, bs, eps = 1024, 3072, 16, 8, 256, 1e-6
+    x = torch.randn((M, H), generator=g).to(BF).to(cuda)
+    wqkv = (torch.randn(((hq + 2 * hkv) * 128, H), generator=g) * 0.05).to(BF).to(cuda)
+    qn = (1 + 0.1 * torch.randn(128, generator=g)).to(BF).to(cuda)
+    kn = (1 + 0.1 * torch.randn(128, generator=g)).to(BF).to(cuda)
+    pos = torch.randint(0, 3000, (M,), generator=g).to(cuda)
+    nb = 2
+    slots = torch.randperm(nb * bs, generator=g)[:M].to(cuda)
+    table = rope_table(4096, 128, 1e6, cuda)
+    caches = [torch.zeros((nb, hkv, bs, 128), dtype=BF, device=cuda) for _ in range(4)]
+    q1 = K().qkv_norm_rope_store(x, wqkv, qn, kn, eps, pos, table, slots, caches[0], caches[1], hq)
+    N = wqkv.shape[0]
+    splits = K().pick_splits(M, N, H)
+    assert splits > 1
+    part = torch.empty((splits, M, N), dtype=torch.float32, device=cuda)
+    K().gemm_splitk(x, wqkv, part, splits)
+    q2 = torch.empty_like(q1)
+    K().splitk_qkv_norm_rope_store(part, splits, qn, kn, eps, pos, table, slots, caches[2], caches[3], hq, q_out=q2)
+    for a, b in ((q1, q2), (caches[0], caches[2]), (caches[1], caches[3])):
+        assert (a.float() - b.float()).abs().max().item() <= 0.07
+        assert (a == b).float().mean().item() > 0.97
+    wgu = interleave_gate_up((torch.randn((I, H), generator=g) * 0.05).to(BF),
+                             (torch.randn((I, H), generator=g) * 0.05).to(BF)).contiguous().to(cuda)
+    a1 = K().gemm_silu_mul(x, wgu)
+    s2 = K().pick_splits(M, 2 * I, H)
+    part2 = torch.empty((s2, M, 2 * I), dtype=torch.float32, device=cuda)
+    K().gemm_splitk(x, wgu, part2, s2)
+    a2 = torch.empty_like(a1)
+    K().splitk_silu_mul(part2, s2, a2)
+    assert (a1.float() - a2.float()).abs().max().item() <= 0.02
+    assert (a1 == a2).float().mean().item() > 0.97
+
+
 @pytest.mark.parametrize("M", [3, 256, 700])
 def test_gemm_silu_mul(cuda, M):
     from awesome_acceleration_b200.runtime import interleave_gate_up
