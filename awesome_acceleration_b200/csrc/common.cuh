@@ -40,7 +40,16 @@ __device__ __forceinline__ void report(unsigned* err, unsigned code) {
 
 // Host-side status helpers (errors.cu).
 int set_error(int status, const char* fmt, ...);
-int check_launch(const char* what);
+int check_launch(const char* what, cudaError_t launch_status = cudaSuccess);
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch (no-ops when the launch did not opt in).
+// griddep_wait: block until the previous kernel in the stream completed and
+// its memory is visible.  griddep_launch: allow the next kernel to begin
+// launching its CTAs.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------
 // bf16 helpers

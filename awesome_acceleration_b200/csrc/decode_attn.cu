@@ -45,6 +45,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
                         float scale_log2, unsigned* err) {
   extern __shared__ uint8_t smem_raw[];
   DecodeSmem& sm = *reinterpret_cast<DecodeSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  griddep_wait();  // q, the new K/V rows and seqlens come from the previous kernels
+  griddep_launch();
 
   const int s = blockIdx.x, h = blockIdx.y;
   const int64_t b = blockIdx.z;
@@ -247,6 +249,8 @@ __global__ void decode_combine_kernel(bf16* __restrict__ out, const float* __res
                                       const float* __restrict__ ws_ml, const int64_t* __restrict__ rows,
                                       const int32_t* __restrict__ seqlens, int ctx_add, int Hq, int64_t max_ctx,
                                       int split_tokens, int max_splits) {
+  griddep_wait();
+  griddep_launch();
   const int hq = blockIdx.x;
   const int64_t b = blockIdx.y;
   int64_t ctx = (int64_t)seqlens[rows[b]] + ctx_add;
@@ -328,13 +332,13 @@ int aacc_paged_decode_attention(const void* q, void* out, const void* k_cache, c
   unsigned* err = device_error_ptr();
   dim3 grid(max_splits, num_kv_heads, (unsigned)batch);
   const size_t smem = decode_smem_bytes();
-#define AACC_LAUNCH_DECODE(GG)                                                                                   \
-  {                                                                                                              \
-    auto kern = paged_decode_kernel<GG>;                                                                         \
-    set_smem_once<paged_decode_kernel<GG>>((int)smem);                                                           \
-    kern<<<grid, kDecodeThreads, smem, stream>>>(tmk, tmv, (const bf16*)q, (bf16*)out, ws_o, ws_ml, block_tables, \
-                                                 max_blocks, slot_indices, seqlens, ctx_add, num_kv_heads,       \
-                                                 block_size, num_blocks, max_context, split_tokens, max_splits, scale_log2, err); \
+  cudaError_t le;
+#define AACC_LAUNCH_DECODE(GG)                                                                                     \
+  {                                                                                                                \
+    set_smem_once<paged_decode_kernel<GG>>((int)smem);                                                             \
+    le = launch_k(paged_decode_kernel<GG>, grid, dim3(kDecodeThreads), smem, stream, tmk, tmv, (const bf16*)q,     \
+                  (bf16*)out, ws_o, ws_ml, block_tables, max_blocks, slot_indices, seqlens, ctx_add, num_kv_heads, \
+                  block_size, num_blocks, max_context, split_tokens, max_splits, scale_log2, err);                 \
   }
   switch (G) {
     case 1: AACC_LAUNCH_DECODE(1) break;
@@ -343,12 +347,13 @@ int aacc_paged_decode_attention(const void* q, void* out, const void* k_cache, c
     default: AACC_LAUNCH_DECODE(8) break;
   }
 #undef AACC_LAUNCH_DECODE
-  st = check_launch("paged_decode_kernel");
+  st = check_launch("paged_decode_kernel", le);
   if (st) return st;
   if (max_splits > 1) {
-    decode_combine_kernel<<<dim3(num_q_heads, (unsigned)batch), kD, 0, stream>>>(
-        (bf16*)out, ws_o, ws_ml, slot_indices, seqlens, ctx_add, num_q_heads, max_context, split_tokens, max_splits);
-    st = check_launch("decode_combine_kernel");
+    st = check_launch("decode_combine_kernel",
+                      launch_k(decode_combine_kernel, dim3(num_q_heads, (unsigned)batch), dim3(kD), 0, stream,
+                               (bf16*)out, (const float*)ws_o, (const float*)ws_ml, slot_indices, seqlens, ctx_add,
+                               num_q_heads, max_context, split_tokens, max_splits));
   }
   return st;
 }

@@ -3,6 +3,7 @@
 #include <cudaTypedefs.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <atomic>
@@ -27,11 +28,20 @@ int set_error(int status, const char* fmt, ...) {
 
 static std::atomic<unsigned long long> g_launches{0};
 
-int check_launch(const char* what) {
+int check_launch(const char* what, cudaError_t launch_status) {
   g_launches.fetch_add(1, std::memory_order_relaxed);
   cudaError_t e = cudaGetLastError();
+  if (launch_status != cudaSuccess) e = launch_status;
   if (e != cudaSuccess) return set_error(AACC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   return AACC_OK;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("AACC_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 
 static std::mutex g_mu;

@@ -310,6 +310,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  griddep_launch();
   const int64_t m0 = (int64_t)blockIdx.y * (128 * MT);
   const int64_t n_base = (int64_t)blockIdx.x * BN;
   // K slabs of this split: [kb0, kb0 + nk).
@@ -343,10 +344,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tma_prefetch_desc(&tma);
     tma_prefetch_desc(&tmb);
     const uint64_t pol_a = policy_evict_last(), pol_b = policy_evict_first();
-    int issued = 0;
-    for (int kb = 0; kb < nk; ++kb) {
+    // The weights (B) do not depend on the previous kernel: start streaming
+    // the first ring's worth of them before waiting for it, then load the
+    // activations (A), which the previous kernel wrote.
+    const int pre = nk < C::STAGES ? nk : C::STAGES;
+    for (int kb = 0; kb < pre; ++kb) {
+      mbar_arrive_expect_tx(&full[kb], C::STAGE_BYTES);
+      tma_load_2d_hint(b_ring + kb * C::B_BYTES, &tmb, &full[kb], (kb0 + kb) * 64, (int)n_base, pol_b);
+    }
+    griddep_wait();
+    for (int kb = 0; kb < pre; ++kb)
+      tma_load_2d_hint(a_ring + kb * C::A_BYTES, &tma, &full[kb], (kb0 + kb) * 64, (int)m0, pol_a);
+    int issued = pre;
+    for (int kb = pre; kb < nk; ++kb) {
       const int st = kb % C::STAGES;
-      if (kb >= C::STAGES && !mbar_wait(&empty[st], ((kb / C::STAGES) - 1) & 1, p.err, abort)) break;
+      if (!mbar_wait(&empty[st], ((kb / C::STAGES) - 1) & 1, p.err, abort)) break;
       mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
       tma_load_2d_hint(a_ring + st * C::A_BYTES, &tma, &full[st], (kb0 + kb) * 64, (int)m0, pol_a);
       tma_load_2d_hint(b_ring + st * C::B_BYTES, &tmb, &full[st], (kb0 + kb) * 64, (int)n_base, pol_b);
@@ -380,6 +392,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   // ---------------- epilogue: all eight warps ----------------
   __syncwarp();
+  griddep_wait();  // outputs may alias buffers the previous kernel still read
   const bool have = mbar_wait(accum, 0, p.err, nullptr);
   tc_fence_after();
   const int quarter = warp & 3, wset = warp >> 2;
@@ -408,6 +421,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 __global__ void argmax_merge_groups_kernel(const float* __restrict__ pv, const int32_t* __restrict__ pi,
                                            int64_t n_groups, int64_t vocab_offset, int64_t* __restrict__ tokens,
                                            float* __restrict__ best_val) {
+  griddep_wait();
+  griddep_launch();
   const int64_t m = blockIdx.x;
   float best = -INFINITY;
   int32_t bi = 0x7fffffff;
@@ -460,8 +475,8 @@ static int launch_gemm(const void* x, const void* w, int64_t M, int64_t N, int64
   auto kern = gemm_tc_kernel<BN, MT, EPI>;
   set_smem_once<gemm_tc_kernel<BN, MT, EPI>>((int)C::SMEM);
   dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + 128 * MT - 1) / (128 * MT)), (unsigned)splits);
-  kern<<<grid, kGemmThreads, C::SMEM, stream>>>(ta, tb, M, N, (int)K, p);
-  return check_launch("gemm_tc_kernel");
+  return check_launch("gemm_tc_kernel",
+                      launch_k(kern, grid, dim3(kGemmThreads), C::SMEM, stream, ta, tb, M, N, (int)K, p));
 }
 
 // Tile shapes: decode batches (M <= 256) use 128x128 tiles, one CTA per
@@ -593,9 +608,10 @@ int aacc_lm_head_argmax(const void* x, const void* w, int64_t M, int64_t vocab, 
   p.err = device_error_ptr();
   st = gemm_dispatch<EPI_ARGMAX>(x, w, M, vocab, K, p, stream);
   if (st) return st;
-  argmax_merge_groups_kernel<<<(unsigned)M, 256, 0, stream>>>(p.part_val, p.part_idx, groups, vocab_offset, tokens,
-                                                              best_val);
-  return check_launch("argmax_merge_groups");
+  return check_launch("argmax_merge_groups",
+                      launch_k(argmax_merge_groups_kernel, dim3((unsigned)M), dim3(256), 0, stream,
+                               (const float*)p.part_val, (const int32_t*)p.part_idx, groups, vocab_offset, tokens,
+                               best_val));
 }
 
 }  // extern "C"

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace aacc {
 
 // Encode a 2-D bf16 tensor map: `inner` contiguous elements per row, `outer`
@@ -13,6 +15,29 @@ int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t ou
                  uint32_t box_inner, uint32_t box_outer, bool swizzle128);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Programmatic dependent launch: every kernel of this library is launched with
+// programmatic stream serialization, so its CTAs may start (shared memory,
+// barriers, TMEM, weight prefetch) while the previous kernel drains; each
+// kernel executes griddepcontrol.wait before touching data the previous
+// kernel produced or consumed.  AACC_PDL=0 in the environment turns it off.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                            Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // Raise a kernel's dynamic shared-memory limit once per device (the call is
 // not a stream operation, so doing it once keeps it out of graph captures).

@@ -10,6 +10,8 @@ __global__ void kv_store_kernel(const bf16* __restrict__ k, const bf16* __restri
                                 int64_t ks, int64_t vs, const int64_t* __restrict__ slot_mapping,
                                 bf16* __restrict__ kc, bf16* __restrict__ vc, int64_t num_slots, int Hkv,
                                 int bs, unsigned* err) {
+  griddep_wait();
+  griddep_launch();
   int64_t warp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   int lane = threadIdx.x & 31;
   if (warp >= T * Hkv) return;
@@ -37,6 +39,8 @@ __global__ void decode_slot_mapping_kernel(const int64_t* __restrict__ rows, con
                                            const int32_t* __restrict__ bt, int64_t max_blocks, int bs,
                                            int64_t num_blocks, int64_t* __restrict__ out, int64_t B,
                                            unsigned* err) {
+  griddep_wait();
+  griddep_launch();
   int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   int64_t row = rows[b];
@@ -58,6 +62,8 @@ __global__ void decode_slot_mapping_kernel(const int64_t* __restrict__ rows, con
 
 __global__ void advance_seqlens_kernel(const int64_t* __restrict__ rows, int32_t* __restrict__ seqlens,
                                        int64_t* __restrict__ positions, int64_t B) {
+  griddep_wait();
+  griddep_launch();
   int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (b < B) {
     atomicAdd(&seqlens[rows[b]], 1);
@@ -68,6 +74,8 @@ __global__ void advance_seqlens_kernel(const int64_t* __restrict__ rows, int32_t
 // dst[i] = src[idx[i]] for rows of `row_bytes` bytes (16-byte multiple).
 __global__ void gather_rows_kernel(const uint4* __restrict__ src, const int64_t* __restrict__ idx, int64_t n_src,
                                    int64_t vec_per_row, uint4* __restrict__ dst, unsigned* err) {
+  griddep_wait();
+  griddep_launch();
   const int64_t i = blockIdx.x;
   int64_t r = idx[i];
   if (r < 0 || r >= n_src) {
@@ -95,10 +103,10 @@ int aacc_kv_store(const void* k, const void* v, int64_t num_tokens, int64_t k_ro
   int64_t warps = num_tokens * num_kv_heads;
   int threads = 256;
   int64_t blocks = (warps + 7) / 8;
-  kv_store_kernel<<<(unsigned)blocks, threads, 0, stream>>>(
-      (const bf16*)k, (const bf16*)v, num_tokens, k_row_stride, v_row_stride, slot_mapping, (bf16*)k_cache,
-      (bf16*)v_cache, num_blocks * block_size, num_kv_heads, block_size, device_error_ptr());
-  return check_launch("kv_store");
+  return check_launch("kv_store", launch_k(kv_store_kernel, dim3((unsigned)blocks), dim3(threads), 0, stream,
+                                           (const bf16*)k, (const bf16*)v, num_tokens, k_row_stride, v_row_stride,
+                                           slot_mapping, (bf16*)k_cache, (bf16*)v_cache, num_blocks * block_size,
+                                           num_kv_heads, block_size, device_error_ptr()));
 }
 
 int aacc_decode_slot_mapping(const int64_t* slot_indices, const int32_t* seqlens, const int32_t* block_tables,
@@ -106,10 +114,10 @@ int aacc_decode_slot_mapping(const int64_t* slot_indices, const int32_t* seqlens
                              int64_t batch, cudaStream_t stream) {
   if (batch < 0 || max_blocks <= 0 || block_size <= 0) return set_error(AACC_ERR_INVALID, "slot_mapping: bad sizes");
   if (batch == 0) return AACC_OK;
-  decode_slot_mapping_kernel<<<(unsigned)((batch + 127) / 128), 128, 0, stream>>>(
-      slot_indices, seqlens, block_tables, max_blocks, block_size, num_blocks, slot_mapping_out, batch,
-      device_error_ptr());
-  return check_launch("decode_slot_mapping");
+  return check_launch("decode_slot_mapping",
+                      launch_k(decode_slot_mapping_kernel, dim3((unsigned)((batch + 127) / 128)), dim3(128), 0,
+                               stream, slot_indices, seqlens, block_tables, max_blocks, block_size, num_blocks,
+                               slot_mapping_out, batch, device_error_ptr()));
 }
 
 int aacc_gather_rows(const void* src, int64_t n_src, int64_t row_bytes, const int64_t* idx, int64_t n, void* dst,
@@ -117,18 +125,17 @@ int aacc_gather_rows(const void* src, int64_t n_src, int64_t row_bytes, const in
   if (n < 0 || n_src <= 0 || row_bytes <= 0 || row_bytes % 16 || !aligned16(src) || !aligned16(dst))
     return set_error(AACC_ERR_INVALID, "gather_rows: rows must be 16-byte multiples and aligned");
   if (n == 0) return AACC_OK;
-  gather_rows_kernel<<<(unsigned)n, 128, 0, stream>>>((const uint4*)src, idx, n_src, row_bytes / 16, (uint4*)dst,
-                                                      device_error_ptr());
-  return check_launch("gather_rows");
+  return check_launch("gather_rows", launch_k(gather_rows_kernel, dim3((unsigned)n), dim3(128), 0, stream,
+                                              (const uint4*)src, idx, n_src, row_bytes / 16, (uint4*)dst,
+                                              device_error_ptr()));
 }
 
 int aacc_advance_seqlens(const int64_t* slot_indices, int32_t* seqlens, int64_t* positions, int64_t batch,
                          cudaStream_t stream) {
   if (batch < 0) return set_error(AACC_ERR_INVALID, "advance_seqlens: bad batch");
   if (batch == 0) return AACC_OK;
-  advance_seqlens_kernel<<<(unsigned)((batch + 127) / 128), 128, 0, stream>>>(slot_indices, seqlens, positions,
-                                                                              batch);
-  return check_launch("advance_seqlens");
+  return check_launch("advance_seqlens", launch_k(advance_seqlens_kernel, dim3((unsigned)((batch + 127) / 128)),
+                                                  dim3(128), 0, stream, slot_indices, seqlens, positions, batch));
 }
 
 }  // extern "C"

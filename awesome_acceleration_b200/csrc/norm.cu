@@ -65,6 +65,8 @@ template <int V>
 __global__ void __launch_bounds__(kNormMaxThreads) rmsnorm_kernel(const bf16* __restrict__ x,
                                                                   const bf16* __restrict__ w, bf16* __restrict__ y,
                                                                   int hidden, float eps) {
+  griddep_wait();
+  griddep_launch();
   const int64_t row = blockIdx.x;
   float v[V * 8];
   load_row<V>(v, x + row * hidden);
@@ -75,6 +77,8 @@ template <int V>
 __global__ void __launch_bounds__(kNormMaxThreads)
     add_rmsnorm_kernel(const bf16* __restrict__ delta, bf16* __restrict__ residual, const bf16* __restrict__ w,
                        bf16* __restrict__ y, int hidden, float eps) {
+  griddep_wait();
+  griddep_launch();
   const int64_t row = blockIdx.x;
   float a[V * 8], d[V * 8];
   load_row<V>(a, residual + row * hidden);
@@ -111,6 +115,8 @@ template <int V>
 __global__ void __launch_bounds__(kNormMaxThreads)
     splitk_add_rmsnorm_kernel(const float* __restrict__ part, int S, int64_t rows, bf16* __restrict__ residual,
                               const bf16* __restrict__ w, bf16* __restrict__ y, int hidden, float eps) {
+  griddep_wait();
+  griddep_launch();
   const int64_t row = blockIdx.x;
   const int64_t stride = rows * hidden;
   float a[V * 8];
@@ -136,6 +142,8 @@ __global__ void __launch_bounds__(kNormMaxThreads)
 
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int S, int64_t n8, int64_t stride,
                                      bf16* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n8) return;
   float d[8];
@@ -153,6 +161,8 @@ __global__ void __launch_bounds__(kNormMaxThreads)
     embed_rmsnorm_kernel(const int64_t* __restrict__ ids, const bf16* __restrict__ table, int64_t vocab,
                          bf16* __restrict__ residual, const bf16* __restrict__ w, bf16* __restrict__ y, int hidden,
                          float eps, unsigned* err) {
+  griddep_wait();
+  griddep_launch();
   const int64_t row = blockIdx.x;
   int64_t id = ids[row];
   if (id < 0 || id >= vocab) {
@@ -185,16 +195,18 @@ static int norm_shape(int64_t rows, int64_t hidden, const char* what, int* threa
 
 using namespace aacc;
 
-#define AACC_NORM_DISPATCH(KERNEL, ...)                                                       \
-  switch (V) {                                                                                \
-    case 1: KERNEL<1><<<(unsigned)rows, threads, 0, stream>>>(__VA_ARGS__); break;            \
-    case 2: KERNEL<2><<<(unsigned)rows, threads, 0, stream>>>(__VA_ARGS__); break;            \
-    case 3: KERNEL<3><<<(unsigned)rows, threads, 0, stream>>>(__VA_ARGS__); break;            \
-    case 4: KERNEL<4><<<(unsigned)rows, threads, 0, stream>>>(__VA_ARGS__); break;            \
-    case 5: KERNEL<5><<<(unsigned)rows, threads, 0, stream>>>(__VA_ARGS__); break;            \
-    case 6: KERNEL<6><<<(unsigned)rows, threads, 0, stream>>>(__VA_ARGS__); break;            \
-    case 7: KERNEL<7><<<(unsigned)rows, threads, 0, stream>>>(__VA_ARGS__); break;            \
-    default: KERNEL<8><<<(unsigned)rows, threads, 0, stream>>>(__VA_ARGS__); break;           \
+#define AACC_NORM_LAUNCH(KV, ...) le = launch_k(KV, dim3((unsigned)rows), dim3(threads), 0, stream, __VA_ARGS__)
+#define AACC_NORM_DISPATCH(KERNEL, ...)                         \
+  cudaError_t le;                                               \
+  switch (V) {                                                  \
+    case 1: AACC_NORM_LAUNCH(KERNEL<1>, __VA_ARGS__); break;    \
+    case 2: AACC_NORM_LAUNCH(KERNEL<2>, __VA_ARGS__); break;    \
+    case 3: AACC_NORM_LAUNCH(KERNEL<3>, __VA_ARGS__); break;    \
+    case 4: AACC_NORM_LAUNCH(KERNEL<4>, __VA_ARGS__); break;    \
+    case 5: AACC_NORM_LAUNCH(KERNEL<5>, __VA_ARGS__); break;    \
+    case 6: AACC_NORM_LAUNCH(KERNEL<6>, __VA_ARGS__); break;    \
+    case 7: AACC_NORM_LAUNCH(KERNEL<7>, __VA_ARGS__); break;    \
+    default: AACC_NORM_LAUNCH(KERNEL<8>, __VA_ARGS__); break;   \
   }
 
 extern "C" {
@@ -204,7 +216,7 @@ int aacc_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t hi
   int st = norm_shape(rows, hidden, "rmsnorm", &threads, &V);
   if (st || rows == 0) return st;
   AACC_NORM_DISPATCH(rmsnorm_kernel, (const bf16*)x, (const bf16*)w, (bf16*)y, (int)hidden, eps)
-  return check_launch("rmsnorm");
+  return check_launch("rmsnorm", le);
 }
 
 int aacc_add_rmsnorm(const void* delta, void* residual, const void* w, void* y, int64_t rows, int64_t hidden, float eps,
@@ -214,7 +226,7 @@ int aacc_add_rmsnorm(const void* delta, void* residual, const void* w, void* y, 
   if (st || rows == 0) return st;
   AACC_NORM_DISPATCH(add_rmsnorm_kernel, (const bf16*)delta, (bf16*)residual, (const bf16*)w, (bf16*)y, (int)hidden,
                      eps)
-  return check_launch("add_rmsnorm");
+  return check_launch("add_rmsnorm", le);
 }
 
 int aacc_splitk_add_rmsnorm(const float* partial, int splits, void* residual, const void* w, void* y, int64_t rows,
@@ -225,7 +237,7 @@ int aacc_splitk_add_rmsnorm(const float* partial, int splits, void* residual, co
   if (splits < 1 || !aligned16(partial)) return set_error(AACC_ERR_INVALID, "splitk_add_rmsnorm: bad partials");
   AACC_NORM_DISPATCH(splitk_add_rmsnorm_kernel, partial, splits, rows, (bf16*)residual, (const bf16*)w, (bf16*)y,
                      (int)hidden, eps)
-  return check_launch("splitk_add_rmsnorm");
+  return check_launch("splitk_add_rmsnorm", le);
 }
 
 int aacc_splitk_reduce(const float* partial, int splits, void* out, int64_t rows, int64_t cols, cudaStream_t stream) {
@@ -233,9 +245,8 @@ int aacc_splitk_reduce(const float* partial, int splits, void* out, int64_t rows
     return set_error(AACC_ERR_INVALID, "splitk_reduce: cols must be a multiple of 8, pointers 16-byte aligned");
   if (rows == 0) return AACC_OK;
   const int64_t n8 = rows * cols / 8;
-  splitk_reduce_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, stream>>>(partial, splits, n8, rows * cols,
-                                                                         (bf16*)out);
-  return check_launch("splitk_reduce");
+  return check_launch("splitk_reduce", launch_k(splitk_reduce_kernel, dim3((unsigned)((n8 + 255) / 256)), dim3(256),
+                                                0, stream, partial, splits, n8, rows * cols, (bf16*)out));
 }
 
 int aacc_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, void* residual, const void* w, void* y,
@@ -246,7 +257,7 @@ int aacc_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, voi
   unsigned* err = device_error_ptr();
   AACC_NORM_DISPATCH(embed_rmsnorm_kernel, ids, (const bf16*)table, vocab, (bf16*)residual, (const bf16*)w, (bf16*)y,
                      (int)hidden, eps, err)
-  return check_launch("embed_rmsnorm");
+  return check_launch("embed_rmsnorm", le);
 }
 
 }  // extern "C"

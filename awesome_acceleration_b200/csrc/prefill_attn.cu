@@ -34,6 +34,8 @@ __global__ void __launch_bounds__(kPThreads, 2)
                         int n_qtiles, float scale_log2, unsigned* err) {
   extern __shared__ uint8_t smem_raw[];
   PrefillSmem& sm = *reinterpret_cast<PrefillSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  griddep_wait();
+  griddep_launch();
   const int qt = n_qtiles - 1 - (int)blockIdx.x;  // heaviest tiles first
   const int hq = blockIdx.y;
   const int64_t s = blockIdx.z;
@@ -243,11 +245,10 @@ int aacc_prefill_attention(const void* q, void* out, const void* k_cache, const 
   const size_t smem = sizeof(PrefillSmem) + 1024;
   set_smem_once<prefill_attn_kernel>((int)smem);
   dim3 grid(n_qtiles, num_q_heads, (unsigned)num_seqs);
-  prefill_attn_kernel<<<grid, kPThreads, smem, stream>>>(tmk, tmv, (const bf16*)q, (bf16*)out, block_tables, max_blocks,
-                                                         seq_rows, cu_q, ctx_start, num_q_heads, num_kv_heads,
-                                                         block_size, num_blocks, n_qtiles, scale * kLog2e,
-                                                         device_error_ptr());
-  return check_launch("prefill_attn_kernel");
+  return check_launch("prefill_attn_kernel",
+                      launch_k(prefill_attn_kernel, grid, dim3(kPThreads), smem, stream, tmk, tmv, (const bf16*)q,
+                               (bf16*)out, block_tables, max_blocks, seq_rows, cu_q, ctx_start, num_q_heads,
+                               num_kv_heads, block_size, num_blocks, n_qtiles, scale * kLog2e, device_error_ptr()));
 }
 
 }  // extern "C"

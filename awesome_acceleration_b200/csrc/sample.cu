@@ -32,6 +32,8 @@ __device__ __forceinline__ void block_argmax(float& bv, int64_t& bi) {
 
 // torch.argmax semantics on bf16 rows: highest value, first index on ties.
 __global__ void argmax_rows_kernel(const bf16* __restrict__ logits, int64_t vocab, int64_t* __restrict__ tokens) {
+  griddep_wait();
+  griddep_launch();
   const int64_t m = blockIdx.x;
   float bv = -INFINITY;
   int64_t bi = INT64_MAX;
@@ -43,6 +45,8 @@ __global__ void argmax_rows_kernel(const bf16* __restrict__ logits, int64_t voca
 
 __global__ void argmax_merge_kernel(const float* __restrict__ cv, const int64_t* __restrict__ ci, int shards,
                                     int64_t* __restrict__ tokens) {
+  griddep_wait();
+  griddep_launch();
   const int64_t m = blockIdx.x;
   float bv = -INFINITY;
   int64_t bi = INT64_MAX;
@@ -61,16 +65,16 @@ extern "C" {
 int aacc_argmax_rows(const void* logits, int64_t M, int64_t vocab, int64_t* tokens, cudaStream_t stream) {
   if (M < 0 || vocab <= 0) return set_error(AACC_ERR_INVALID, "argmax_rows: bad sizes");
   if (M == 0) return AACC_OK;
-  argmax_rows_kernel<<<(unsigned)M, 512, 0, stream>>>((const bf16*)logits, vocab, tokens);
-  return check_launch("argmax_rows");
+  return check_launch("argmax_rows", launch_k(argmax_rows_kernel, dim3((unsigned)M), dim3(512), 0, stream,
+                                              (const bf16*)logits, vocab, tokens));
 }
 
 int aacc_argmax_merge(const float* cand_val, const int64_t* cand_idx, int64_t M, int shards, int64_t* tokens,
                       cudaStream_t stream) {
   if (M < 0 || shards <= 0) return set_error(AACC_ERR_INVALID, "argmax_merge: bad sizes");
   if (M == 0) return AACC_OK;
-  argmax_merge_kernel<<<(unsigned)M, 32, 0, stream>>>(cand_val, cand_idx, shards, tokens);
-  return check_launch("argmax_merge");
+  return check_launch("argmax_merge", launch_k(argmax_merge_kernel, dim3((unsigned)M), dim3(32), 0, stream, cand_val,
+                                               cand_idx, shards, tokens));
 }
 
 }  // extern "C"

@@ -21,6 +21,8 @@ __global__ void __launch_bounds__(128)
                       const bf16* __restrict__ rope, int64_t max_pos, const int64_t* __restrict__ slot_mapping,
                       bf16* __restrict__ q_out, bf16* __restrict__ k_cache, bf16* __restrict__ v_cache,
                       int64_t num_slots, int Hq, int Hkv, int bs, unsigned* err) {
+  griddep_wait();
+  griddep_launch();
   const int heads = Hq + 2 * Hkv;
   const int64_t item = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
   if (item >= M * heads) return;
@@ -84,6 +86,8 @@ __global__ void __launch_bounds__(128)
 __global__ void splitk_silu_kernel(const float* __restrict__ part, int S, int64_t M, int64_t I,
                                    bf16* __restrict__ out) {
   // one thread = 8 consecutive output columns of one row
+  griddep_wait();
+  griddep_launch();
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t per_row = I / 8;
   if (t >= M * per_row) return;
@@ -136,11 +140,12 @@ int aacc_splitk_qkv_norm_rope_store(const float* partial, int splits, const void
   if (!aligned16(partial) || !aligned16(q_out) || !aligned16(k_cache) || !aligned16(v_cache))
     return set_error(AACC_ERR_INVALID, "splitk_qkv_norm_rope_store: pointers must be 16-byte aligned");
   const int64_t items = M * (num_q_heads + 2 * num_kv_heads);
-  splitk_qkv_kernel<<<(unsigned)((items + 3) / 4), 128, 0, stream>>>(
-      partial, splits, M, (const bf16*)q_norm_w, (const bf16*)k_norm_w, eps, positions, (const bf16*)rope_cos_sin,
-      max_pos, slot_mapping, (bf16*)q_out, (bf16*)k_cache, (bf16*)v_cache, num_blocks * block_size, num_q_heads,
-      num_kv_heads, block_size, device_error_ptr());
-  return check_launch("splitk_qkv_norm_rope_store");
+  return check_launch(
+      "splitk_qkv_norm_rope_store",
+      launch_k(splitk_qkv_kernel, dim3((unsigned)((items + 3) / 4)), dim3(128), 0, stream, partial, splits, M,
+               (const bf16*)q_norm_w, (const bf16*)k_norm_w, eps, positions, (const bf16*)rope_cos_sin, max_pos,
+               slot_mapping, (bf16*)q_out, (bf16*)k_cache, (bf16*)v_cache, num_blocks * block_size, num_q_heads,
+               num_kv_heads, block_size, device_error_ptr()));
 }
 
 int aacc_splitk_silu_mul(const float* partial, int splits, void* out, int64_t M, int64_t I, cudaStream_t stream) {
@@ -148,8 +153,8 @@ int aacc_splitk_silu_mul(const float* partial, int splits, void* out, int64_t M,
     return set_error(AACC_ERR_INVALID, "splitk_silu_mul: I must be a multiple of 64, pointers 16-byte aligned");
   if (M == 0) return AACC_OK;
   const int64_t n = M * I / 8;
-  splitk_silu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(partial, splits, M, I, (bf16*)out);
-  return check_launch("splitk_silu_mul");
+  return check_launch("splitk_silu_mul", launch_k(splitk_silu_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256),
+                                                  0, stream, partial, splits, M, I, (bf16*)out));
 }
 
 }  // extern "C"

@@ -140,6 +140,8 @@ class Cfg2:
         self.n_seqs = 32 if args.small else 256
         self.prompt = 256 if args.small else 1024
         self.out = 64 if args.small else 1024
+        if args.midrun:  # profiler captures: the job's mean decode context, a few steps
+            self.prompt, self.out = 1536, 8
         self.seed = 1234 + args.rank
 
 
@@ -382,6 +384,82 @@ def run_attn(args, device):
             "gpu_launches": 2 * args.steps, "clocks": clk.summary()}
 
 
+# --------------------------------------------------------------------------- cfg4: Qwen3-8B tensor parallel
+def run_cfg4(args, device):
+    """Qwen3-8B architecture (random-init bf16), 128 seqs x
+    2048 prompt tokens, 512 greedy outputs, tensor parallel over the torchrun
+    world (TP = --tp, DP = world / TP replicas).  Every rank of a TP group runs
+    the same device job; each decode step is one CUDA graph holding the
+    RowParallel all-reduces and the vocab-parallel argmax all-gather."""
+    from awesome_acceleration_b200 import _lib
+    from awesome_acceleration_b200.llm_tp import LLMTP
+    from awesome_acceleration_b200.model.model import Qwen3Config
+    tp = args.tp or args.world
+    cfg = Qwen3Config(hidden_size=4096, intermediate_size=12288, num_hidden_layers=36, num_attention_heads=32,
+                      num_key_value_heads=8, tie_word_embeddings=False)
+    n_seqs, prompt, out = (16, 512, 32) if args.small else (128, 2048, 512)
+    llm = LLMTP(None, max_num_seqs=n_seqs, max_seq_len=prompt + out + 16, enable_tp=args.world > 1, tp_size=tp,
+                config=cfg, seed=7)
+    dp = llm.dp_size
+    prompts = make_prompts(n_seqs, prompt, cfg.vocab_size, 4321 + llm.dp_rank)
+
+    class C:
+        pass
+    c = C()
+    c.n_seqs, c.prompt, c.out = n_seqs, prompt, out
+    lib = _lib.load()
+    rt = llm.model._rt()
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        rows = device_job(llm, prompts, out)
+        torch.cuda.synchronize()
+        reset_job(llm, rows)
+    _lib.raise_on_device_error("warm-up")
+    barrier(args)
+    torch.cuda.synchronize()
+    n0, r0 = lib.aacc_launch_count(), rt.graph_replays
+    e0, e1, em = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    elapsed = prefill_s = 0.0
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        for _ in range(args.steps):
+            e0.record(stream)
+            rows = device_job(llm, prompts, out, mark=em)
+            e1.record(stream)
+            e1.synchronize()
+            elapsed += e0.elapsed_time(e1) / 1e3
+            prefill_s += e0.elapsed_time(em) / 1e3
+            reset_job(llm, rows)
+    _lib.raise_on_device_error("timed region")
+    launches = lib.aacc_launch_count() - n0 + (rt.graph_replays - r0) * rt.graph_launches.get(n_seqs, 0)
+    t_max = max_over_ranks(args, elapsed)
+    value = dp * n_seqs * out * args.steps / t_max
+    pk, kind = peaks()
+    n_dec = out - 1
+    kv_tok = 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * 128 * 2 // tp
+    w_bytes = (36 * (4096 * 6144 + 4096 * 4096 + 3 * 4096 * 12288) + cfg.vocab_size * 4096) * 2 / tp
+    ctx = prompt + 1 + np.arange(n_dec)
+    dec_bytes = n_dec * w_bytes + n_seqs * kv_tok * float(ctx.sum() + n_dec)
+    decode_s = (elapsed - prefill_s) / args.steps
+    llm_stop = getattr(llm, "stop", None)
+    if llm_stop:
+        llm_stop()
+    return {
+        "metric": f"output tok/s (Qwen3-8B, {n_seqs}x{prompt} in / {out} out, greedy, TP{tp} x DP{dp})",
+        "value": round(value, 1), "unit": "output tok/s", "n_gpus": args.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(t_max / args.steps * 1e3, 2), "higher_is_better": True,
+        "scaling": "strong" if dp == 1 else "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (uniform random token ids, random-init weights)",
+        "config": {"workload": "cfg4: Qwen3-8B TP" + (" [SMALL]" if args.small else ""), "global_batch": n_seqs * dp,
+                   "seq_len": prompt + out, "parallelism": f"tp{tp}" + (f"xdp{dp}" if dp > 1 else ""),
+                   "l2": "inputs larger than L2"},
+        "gpu_launches": int(launches), "clocks": clk.summary(),
+        "phases": {"prefill_ms": round(prefill_s / args.steps * 1e3, 1), "decode_ms": round(decode_s * 1e3, 1),
+                   "decode_ms_per_step": round(decode_s / n_dec * 1e3, 3),
+                   "decode_roofline_frac_per_gpu": round(dec_bytes / (pk["hbm_gbs"] * 1e9) / decode_s, 3),
+                   "peak_kind": kind},
+    }
+
+
 # --------------------------------------------------------------------------- prefill GEMMs (tensor pipe)
 def run_gemm(args, device):
     """The four cfg2 projections on one prefill chunk (M tokens) or, with
@@ -494,10 +572,13 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "attn", "gemm"])
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg4", "attn", "gemm"])
+    ap.add_argument("--tp", type=int, default=0, help="cfg4: tensor-parallel size (default: the whole world)")
     ap.add_argument("--small", action="store_true", help="small case for profiler captures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--decode", action="store_true", help="gemm workload: decode-batch shapes")
+    ap.add_argument("--midrun", action="store_true",
+                    help="cfg2 profiler case: 1536-token prompts (the job's mean decode context), 7 decode steps")
     ap.add_argument("--profile", action="store_true",
                     help="profiler capture: warm-up + timed jobs only (no roofline/e2e/CPU legs)")
     args = ap.parse_args()
@@ -515,7 +596,7 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                              device_id=device)
     try:
-        line = {"attn": run_attn, "gemm": run_gemm, "cfg2": run_cfg2}[args.workload](args, device)
+        line = {"attn": run_attn, "gemm": run_gemm, "cfg2": run_cfg2, "cfg4": run_cfg4}[args.workload](args, device)
         if args.rank == 0 and args.workload == "cfg2" and not (args.no_cpu_baseline or args.profile):
             v, info = cpu_sample()
             line["cpu_baseline"] = {"value": round(v, 3), "unit": "output tok/s", "cores": info["cores"],

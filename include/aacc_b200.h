@@ -144,7 +144,13 @@ int aacc_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, voi
 
 /* ---- GEMMs (tcgen05 / TMEM, TMA-fed) --------------------------------------
  * x: [M][K] activations, w: [N][K] weights (nn.Linear layout); K multiple
- * of 64; fp32 accumulation, bf16 outputs. */
+ * of 64; fp32 accumulation, bf16 outputs.
+ *
+ * All kernels of this library use programmatic dependent launch: a kernel
+ * may start while the previous kernel on the stream drains, and waits for
+ * it before touching its data.  The GEMMs start streaming `w` before that
+ * wait, so `w` must be a weight, i.e. not written by the kernel launched
+ * immediately before on the same stream.  AACC_PDL=0 disables the overlap. */
 
 /* out[M][N] = x @ w^T.  nn.Linear / F.linear (o_proj model/model.py:258,
  * down_proj :190, RowParallelLinear parallel_layers.py:190). */

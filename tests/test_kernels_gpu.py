@@ -302,7 +302,9 @@ def test_splitk_qkv_and_silu_epilogues(cuda, M):
     K().gemm_splitk(x, wgu, part2, s2)
     a2 = torch.empty_like(a1)
     K().splitk_silu_mul(part2, s2, a2)
-    assert (a1.float() - a2.float()).abs().max().item() <= 0.02
+    mag = torch.maximum(a1.float().abs(), a2.float().abs())
+    # a 1-ulp difference in gate or up moves the product by at most 2 bf16 ulps
+    assert ((a1.float() - a2.float()).abs() <= mag * 2 ** -6 + 1e-3).all()
     assert (a1 == a2).float().mean().item() > 0.97
 
 
