@@ -8,8 +8,10 @@
 // mma.sync m16n8k16 (the G query heads that share the kv head are the rows of
 // the A operand), keeping an online softmax in fp32.  The four partial
 // (max, sum, O) triples are merged in shared memory; a split either writes
-// the final bf16 output (single split) or an fp32 partial that
-// decode_combine_kernel merges.
+// the final bf16 output (single split) or an fp32 partial, and the last
+// split CTA of a (sequence, kv head) to finish, found with an atomic counter
+// in the workspace, merges the partials in split order and resets the
+// counter (no separate combine launch).
 //
 // The kernel is HBM-bound: each K/V byte of the context is read once per
 // kv head.  Algorithmic bytes per call = sum(ctx) * Hkv * 128 * 2 * 2.
@@ -42,7 +44,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
                         float* __restrict__ ws_ml, const int32_t* __restrict__ bt, int64_t max_blocks,
                         const int64_t* __restrict__ rows, const int32_t* __restrict__ seqlens, int ctx_add,
                         int Hkv, int bs, int64_t num_blocks, int64_t max_ctx, int split_tokens, int max_splits,
-                        float scale_log2, unsigned* err) {
+                        float scale_log2, int* __restrict__ cnt, unsigned* err) {
   extern __shared__ uint8_t smem_raw[];
   DecodeSmem& sm = *reinterpret_cast<DecodeSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   griddep_wait();  // q, the new K/V rows and seqlens come from the previous kernels
@@ -242,33 +244,36 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
       }
     }
   }
-}
-
-// Merge the per-split partials of rows whose context needed more than one split.
-__global__ void decode_combine_kernel(bf16* __restrict__ out, const float* __restrict__ ws_o,
-                                      const float* __restrict__ ws_ml, const int64_t* __restrict__ rows,
-                                      const int32_t* __restrict__ seqlens, int ctx_add, int Hq, int64_t max_ctx,
-                                      int split_tokens, int max_splits) {
-  griddep_wait();
-  griddep_launch();
-  const int hq = blockIdx.x;
-  const int64_t b = blockIdx.y;
-  int64_t ctx = (int64_t)seqlens[rows[b]] + ctx_add;
-  if (ctx > max_ctx) ctx = max_ctx;
-  const int n_splits = (int)((ctx + split_tokens - 1) / split_tokens);
-  if (n_splits <= 1) return;
-  const int64_t qh = b * Hq + hq;
-  const int d = threadIdx.x;
-  float M = -INFINITY;
-  for (int s = 0; s < n_splits; ++s) M = fmaxf(M, ws_ml[(qh * max_splits + s) * 2]);
-  const float Mu = (M == -INFINITY) ? 0.f : M;
-  float L = 0.f, O = 0.f;
-  for (int s = 0; s < n_splits; ++s) {
-    const float f = exp2f(ws_ml[(qh * max_splits + s) * 2] - Mu);
-    L += f * ws_ml[(qh * max_splits + s) * 2 + 1];
-    O += f * ws_o[(qh * max_splits + s) * kD + d];
+  if (n_splits == 1 || cnt == nullptr) return;
+  // The last split CTA of this (sequence, kv head) to finish merges all
+  // splits (threadfence-reduction pattern) and resets the counter to zero.
+  __threadfence();
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32));
+  __shared__ int s_last;
+  if (d == 0) {
+    const int prev = atomicAdd(&cnt[b * Hkv + h], 1);
+    s_last = (prev == n_splits - 1);
   }
-  out[qh * kD + d] = tobf(L > 0.f ? O / L : 0.f);
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32));
+  if (!s_last) return;
+  __threadfence();
+#pragma unroll
+  for (int gg = 0; gg < G; ++gg) {
+    const int64_t qh = b * Hq + (int64_t)h * G + gg;
+    const volatile float* ml = ws_ml + qh * max_splits * 2;
+    const volatile float* po = ws_o + qh * max_splits * kD;
+    float M = -INFINITY;
+    for (int t = 0; t < n_splits; ++t) M = fmaxf(M, ml[2 * t]);
+    const float Mu = (M == -INFINITY) ? 0.f : M;
+    float L = 0.f, O = 0.f;
+    for (int t = 0; t < n_splits; ++t) {
+      const float f = exp2f(ml[2 * t] - Mu);
+      L += f * ml[2 * t + 1];
+      O += f * po[t * kD + d];
+    }
+    out[qh * kD + d] = tobf(L > 0.f ? O / L : 0.f);
+  }
+  if (d == 0) cnt[b * Hkv + h] = 0;
 }
 
 static int default_split(int64_t batch, int Hkv, int64_t max_ctx) {
@@ -293,7 +298,9 @@ int64_t aacc_paged_decode_workspace_bytes(int64_t batch, int num_q_heads, int64_
   if (split_tokens <= 0) split_tokens = default_split(batch, 1, max_context);  // upper bound on splits
   int64_t max_splits = (max_context + split_tokens - 1) / split_tokens;
   if (max_splits < 1) max_splits = 1;
-  return batch * num_q_heads * max_splits * (kD + 2) * (int64_t)sizeof(float);
+  // partial O | partial (max, sum) | one merge counter per (row, kv head) (<= q heads)
+  return batch * num_q_heads * max_splits * (kD + 2) * (int64_t)sizeof(float) +
+         batch * num_q_heads * (int64_t)sizeof(int);
 }
 
 int aacc_paged_decode_attention(const void* q, void* out, const void* k_cache, const void* v_cache, int64_t num_blocks,
@@ -316,7 +323,8 @@ int aacc_paged_decode_attention(const void* q, void* out, const void* k_cache, c
   if (split_tokens % kTile) return set_error(AACC_ERR_INVALID, "split_tokens must be a multiple of %d", kTile);
   const int max_splits = (int)((max_context + split_tokens - 1) / split_tokens);
   if (max_splits > 1) {
-    const int64_t need = batch * num_q_heads * (int64_t)max_splits * (kD + 2) * (int64_t)sizeof(float);
+    const int64_t need = batch * num_q_heads * (int64_t)max_splits * (kD + 2) * (int64_t)sizeof(float) +
+                         batch * num_kv_heads * (int64_t)sizeof(int);
     if (!workspace || workspace_bytes < need)
       return set_error(AACC_ERR_INVALID, "paged_decode_attention: workspace %lld < %lld bytes",
                        (long long)workspace_bytes, (long long)need);
@@ -328,6 +336,7 @@ int aacc_paged_decode_attention(const void* q, void* out, const void* k_cache, c
   if (st) return st;
   float* ws_o = static_cast<float*>(workspace);
   float* ws_ml = ws_o ? ws_o + batch * num_q_heads * (int64_t)max_splits * kD : nullptr;
+  int* cnt = ws_ml ? reinterpret_cast<int*>(ws_ml + batch * num_q_heads * (int64_t)max_splits * 2) : nullptr;
   const float scale_log2 = scale * kLog2e;
   unsigned* err = device_error_ptr();
   dim3 grid(max_splits, num_kv_heads, (unsigned)batch);
@@ -338,7 +347,7 @@ int aacc_paged_decode_attention(const void* q, void* out, const void* k_cache, c
     set_smem_once<paged_decode_kernel<GG>>((int)smem);                                                             \
     le = launch_k(paged_decode_kernel<GG>, grid, dim3(kDecodeThreads), smem, stream, tmk, tmv, (const bf16*)q,     \
                   (bf16*)out, ws_o, ws_ml, block_tables, max_blocks, slot_indices, seqlens, ctx_add, num_kv_heads, \
-                  block_size, num_blocks, max_context, split_tokens, max_splits, scale_log2, err);                 \
+                  block_size, num_blocks, max_context, split_tokens, max_splits, scale_log2, cnt, err);            \
   }
   switch (G) {
     case 1: AACC_LAUNCH_DECODE(1) break;
@@ -347,15 +356,7 @@ int aacc_paged_decode_attention(const void* q, void* out, const void* k_cache, c
     default: AACC_LAUNCH_DECODE(8) break;
   }
 #undef AACC_LAUNCH_DECODE
-  st = check_launch("paged_decode_kernel", le);
-  if (st) return st;
-  if (max_splits > 1) {
-    st = check_launch("decode_combine_kernel",
-                      launch_k(decode_combine_kernel, dim3(num_q_heads, (unsigned)batch), dim3(kD), 0, stream,
-                               (bf16*)out, (const float*)ws_o, (const float*)ws_ml, slot_indices, seqlens, ctx_add,
-                               num_q_heads, max_context, split_tokens, max_splits));
-  }
-  return st;
+  return check_launch("paged_decode_kernel", le);
 }
 
 }  // extern "C"

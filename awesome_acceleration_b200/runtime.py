@@ -106,7 +106,7 @@ class _DecodeBuffers:
         self.attn = torch.zeros((B, Hq, 128), **bf)
         self.act = torch.zeros((B, I), **bf)
         ws = K.decode_workspace_bytes(B, Hq, max_context)
-        self.attn_ws = torch.empty(max(ws, 16), dtype=torch.uint8, device=device)
+        self.attn_ws = torch.zeros(max(ws, 16), dtype=torch.uint8, device=device)  # zeroed merge counters
         self.lm_ws = torch.empty(K.lm_head_workspace_bytes(B, vocab), dtype=torch.uint8, device=device)
         self.best = torch.zeros(B, dtype=torch.float32, device=device)
         self.tok = torch.zeros(B, **i64)

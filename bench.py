@@ -345,7 +345,7 @@ def run_attn(args, device):
     seqlens = torch.tensor(ctx, dtype=torch.int32, device=device) - 1
     rows = torch.arange(B, dtype=torch.int64, device=device)
     btd = bt.to(device)
-    ws = torch.empty(Kk.decode_workspace_bytes(B, hq, maxb * bs), dtype=torch.uint8, device=device)
+    ws = torch.zeros(Kk.decode_workspace_bytes(B, hq, maxb * bs), dtype=torch.uint8, device=device)
     out = torch.empty_like(q)
     # slot mapping of the new token (1 per sequence) + its store, as in a decode step
     stream = torch.cuda.current_stream()

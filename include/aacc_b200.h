@@ -82,7 +82,8 @@ int aacc_gather_rows(const void* src, int64_t n_src, int64_t row_bytes, const in
 /* ---- attention ----------------------------------------------------------- */
 
 /* Workspace bytes aacc_paged_decode_attention needs for `batch` rows with at
- * most `max_context` tokens each. */
+ * most `max_context` tokens each.  The workspace must be zero-filled before
+ * its first use (it holds merge counters that every call leaves at zero). */
 int64_t aacc_paged_decode_workspace_bytes(int64_t batch, int num_q_heads, int64_t max_context,
                                           int split_tokens);
 

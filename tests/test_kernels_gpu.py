@@ -142,7 +142,7 @@ def test_paged_decode_attention(cuda, G, hkv):
     q = (torch.randn((B, hq, 128), generator=g) / math.sqrt(128)).to(BF)
     scale = 128 ** -0.5
     max_ctx = bt.shape[1] * bs
-    ws = torch.empty(K().decode_workspace_bytes(B, hq, max_ctx, 64), dtype=torch.uint8, device=cuda)
+    ws = torch.zeros(K().decode_workspace_bytes(B, hq, max_ctx, 64), dtype=torch.uint8, device=cuda)
     clear_err()
     for split in (0, 64, 512):
         out = K().paged_decode_attention(q.to(cuda), kp.to(cuda), vp.to(cuda), bt_rows.to(cuda),
