@@ -51,9 +51,10 @@ def test_llm_stops_on_eos_and_max_seq_len(cuda):
     sd = init_weights(TINY, 42, norm_jitter=0.1)
     llm = LLM(model=_model(sd), max_num_seqs=2, max_seq_len=70)
     prompt = random_prompts(1, 60, TINY.vocab_size, 43)[0]
-    # pos >= max_seq_len stops generation (llm.py:417): 60-token prompt, limit 70
+    # pos >= max_seq_len stops generation (llm.py:417): 60-token prompt, limit 70:
+    # the prefill token plus decode steps at positions 60..69 -> 11 tokens
     out = llm.generate_ids([prompt], max_tokens=100, ignore_eos=True).result(timeout=60)[0]
-    assert out.generated_tokens == 10
+    assert out.generated_tokens == 11
     # EOS: make the first generated token the EOS id and check the stop
     # (the loop reads the EOS id when it starts; stop it first)
     first = out.token_ids[0]
