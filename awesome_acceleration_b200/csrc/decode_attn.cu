@@ -15,6 +15,8 @@
 //
 // The kernel is HBM-bound: each K/V byte of the context is read once per
 // kv head.  Algorithmic bytes per call = sum(ctx) * Hkv * 128 * 2 * 2.
+#include <mutex>
+
 #include "common.cuh"
 #include "host.h"
 
@@ -357,6 +359,94 @@ int aacc_paged_decode_attention(const void* q, void* out, const void* k_cache, c
   }
 #undef AACC_LAUNCH_DECODE
   return check_launch("paged_decode_kernel", le);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// Some callers cannot allocate device memory at all: a plugin run by a host
+// runtime that owns every device allocation and forbids its plugins to call
+// cudaMalloc, or a service that must keep a fixed device-memory footprint
+// after start-up.  For them aacc_paged_decode_attention_noalloc takes no
+// workspace: its split partials and merge counters live in the file-scope
+// array below, of fixed size kNoAllocScratchBytes, which every GPU that loads
+// this library holds until the process exits.  The first call on a device
+// (with that device current) looks up the array's device address with
+// cudaGetSymbolAddress, so make that first call before any stream capture.
+// Every call on a device shares the one array and leaves its last contents
+// behind; the merge counters, the only part that must start at zero, are
+// cleared on the caller's stream before each launch.  Calls that overlap on
+// the GPU (different streams, concurrently) race on the array.
+// ---------------------------------------------------------------------------
+namespace aacc {
+
+constexpr int64_t kNoAllocScratchBytes = int64_t(16) << 20;  // 16 MiB
+static __device__ __align__(256) unsigned char g_decode_noalloc_scratch[kNoAllocScratchBytes];
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[64];
+
+static int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64)
+    return set_error(AACC_ERR_CUDA, "paged_decode_attention_noalloc: no current device (%s)",
+                     cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(AACC_ERR_CUDA, "paged_decode_attention_noalloc: cudaGetSymbolAddress failed: %s",
+                       cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return AACC_OK;
+}
+
+}  // namespace aacc
+
+extern "C" {
+
+int64_t aacc_paged_decode_noalloc_capacity_bytes(void) { return kNoAllocScratchBytes; }
+
+int aacc_paged_decode_attention_noalloc(const void* q, void* out, const void* k_cache, const void* v_cache,
+                                        int64_t num_blocks, const int32_t* block_tables, int64_t max_blocks,
+                                        const int64_t* slot_indices, const int32_t* seqlens, int ctx_add,
+                                        int64_t batch, int num_q_heads, int num_kv_heads, int block_size,
+                                        float scale, int split_tokens, int64_t max_context, cudaStream_t stream) {
+  if (batch < 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads || block_size <= 0 ||
+      max_blocks <= 0 || max_context <= 0)
+    return set_error(AACC_ERR_INVALID, "paged_decode_attention_noalloc: bad sizes");
+  if (batch == 0) return AACC_OK;
+  // The same split plan as aacc_paged_decode_attention, to size the scratch.
+  int64_t ctx = max_context > max_blocks * block_size ? max_blocks * block_size : max_context;
+  const int split = split_tokens > 0 ? split_tokens : default_split(batch, num_kv_heads, ctx);
+  if (split % kTile) return set_error(AACC_ERR_INVALID, "split_tokens must be a multiple of %d", kTile);
+  const int64_t max_splits = (ctx + split - 1) / split;
+  const int64_t partial_bytes = batch * num_q_heads * max_splits * (kD + 2) * (int64_t)sizeof(float);
+  const int64_t counter_bytes = batch * num_kv_heads * (int64_t)sizeof(int);
+  if (max_splits > 1 && partial_bytes + counter_bytes > kNoAllocScratchBytes)
+    return set_error(AACC_ERR_INVALID,
+                     "paged_decode_attention_noalloc: %lld rows x %d q heads x %lld splits need %lld bytes of "
+                     "scratch; the static scratch holds %lld bytes (use aacc_paged_decode_attention with a "
+                     "workspace, or fewer rows / a larger split_tokens)",
+                     (long long)batch, num_q_heads, (long long)max_splits,
+                     (long long)(partial_bytes + counter_bytes), (long long)kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  int st = noalloc_scratch(&scratch);
+  if (st) return st;
+  if (max_splits > 1) {
+    cudaError_t e = cudaMemsetAsync(static_cast<char*>(scratch) + partial_bytes, 0, counter_bytes, stream);
+    if (e != cudaSuccess)
+      return set_error(AACC_ERR_CUDA, "paged_decode_attention_noalloc: clearing counters: %s", cudaGetErrorString(e));
+  }
+  return aacc_paged_decode_attention(q, out, k_cache, v_cache, num_blocks, block_tables, max_blocks, slot_indices,
+                                     seqlens, ctx_add, batch, num_q_heads, num_kv_heads, block_size, scale, split,
+                                     ctx, scratch, kNoAllocScratchBytes, stream);
 }
 
 }  // extern "C"

@@ -100,6 +100,26 @@ int aacc_paged_decode_attention(const void* q, void* out, const void* k_cache, c
                                 float scale, int split_tokens, int64_t max_context, void* workspace,
                                 int64_t workspace_bytes, cudaStream_t stream);
 
+/* Allocation-free variant of aacc_paged_decode_attention (same arguments
+ * minus the workspace), for callers that cannot allocate device memory, such
+ * as plugins under a host runtime that owns all device allocations, or
+ * services that keep a fixed device footprint after start-up.  Its scratch
+ * (split partials + merge counters) is a static 16 MiB array inside this
+ * library, held by every GPU that loads it; calls whose split plan needs more
+ * (aacc_paged_decode_noalloc_capacity_bytes) fail with AACC_ERR_INVALID.
+ * The first call on a device, with that device current, looks up the array's
+ * address; make it before any stream capture.  All calls on a device share the
+ * array (the counters are cleared on the caller's stream each call), so calls
+ * that overlap on the GPU race.  No counterpart in the reference. */
+int aacc_paged_decode_attention_noalloc(const void* q, void* out, const void* k_cache, const void* v_cache,
+                                        int64_t num_blocks, const int32_t* block_tables, int64_t max_blocks,
+                                        const int64_t* slot_indices, const int32_t* seqlens, int ctx_add,
+                                        int64_t batch, int num_q_heads, int num_kv_heads, int block_size,
+                                        float scale, int split_tokens, int64_t max_context, cudaStream_t stream);
+
+/* Bytes of static scratch aacc_paged_decode_attention_noalloc can use. */
+int64_t aacc_paged_decode_noalloc_capacity_bytes(void);
+
 /* Causal (chunked) prefill attention over the paged cache.  Sequence s owns
  * query rows [cu_q[s], cu_q[s+1]) of q/out ([T][num_q_heads][128]) at
  * positions ctx_start[s] + i; its K/V (earlier chunks and this chunk) are
