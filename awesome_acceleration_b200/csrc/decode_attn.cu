@@ -92,6 +92,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
       tma_prefetch_desc(&tmk);
       tma_prefetch_desc(&tmv);
       const int32_t* btrow = bt + row * max_blocks;
+      // K/V tiles are read exactly once: evict_first keeps them from
+      // displacing the projection weights held in L2 across the attention.
+      const uint64_t pol = policy_evict_first();
       int issued = 0;
       for (int i = 0; i < ntiles; ++i) {
         const int st = i % kDecodeStages;
@@ -104,10 +107,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
         }
         const int r = (int)((blk * Hkv + h) * bs + t0 % bs);
         mbar_arrive_expect_tx(&sm.full[st], 4 * kHalfTileBytes);
-        tma_load_2d(sm.tiles[st][0], &tmk, &sm.full[st], 0, r);
-        tma_load_2d(sm.tiles[st][1], &tmk, &sm.full[st], 64, r);
-        tma_load_2d(sm.tiles[st][2], &tmv, &sm.full[st], 0, r);
-        tma_load_2d(sm.tiles[st][3], &tmv, &sm.full[st], 64, r);
+        tma_load_2d_hint(sm.tiles[st][0], &tmk, &sm.full[st], 0, r, pol);
+        tma_load_2d_hint(sm.tiles[st][1], &tmk, &sm.full[st], 64, r, pol);
+        tma_load_2d_hint(sm.tiles[st][2], &tmv, &sm.full[st], 0, r, pol);
+        tma_load_2d_hint(sm.tiles[st][3], &tmv, &sm.full[st], 64, r, pol);
         ++issued;
       }
       // Drain: every copy this CTA issued has landed before the CTA may exit.
