@@ -51,6 +51,12 @@ SIGNATURES: dict[str, tuple] = {
     "aacc_lm_head_argmax": (I32, [P, P, I64, I64, I64, I64, P, P, P, P, I64, P]),
     "aacc_argmax_rows": (I32, [P, I64, I64, P, P]),
     "aacc_argmax_merge": (I32, [P, P, I64, I32, P, P]),
+    "aacc_tp_exchange_bytes": (I64, [I32, I64, I64]),
+    "aacc_peer_buffer_alloc": (I32, [I64, P, P]),
+    "aacc_peer_buffer_open": (I32, [P, P]),
+    "aacc_peer_buffer_close": (I32, [P]),
+    "aacc_peer_buffer_free": (I32, [P]),
+    "aacc_tp_allreduce_add_rmsnorm": (I32, [P, I32, P, I32, I32, I32, I64, P, P, P, I64, I64, F32, P]),
 }
 
 _lib = None

@@ -30,6 +30,7 @@ enum DeviceErr : unsigned {
   ERR_POS_OOB = 8u,        // position outside the RoPE table
   ERR_TOKEN_OOB = 16u,     // token id outside the vocabulary
   ERR_CTX_OOB = 32u,       // context longer than the block table row
+  ERR_PEER_TIMEOUT = 64u,  // a peer GPU's arrival flag did not come within the time limit
 };
 
 unsigned* device_error_ptr();  // host: device address of the error word (current device)

@@ -6,6 +6,8 @@ capture.  Outputs are allocated here only when the caller passes none.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -237,3 +239,44 @@ def argmax_merge(cand_val, cand_idx, tokens=None):
         tokens = torch.empty(M, dtype=torch.int64, device=cand_val.device)
     _lib.check(_lib_().aacc_argmax_merge(_p(cand_val), _p(cand_idx), M, S, _p(tokens), _stream()), "argmax_merge")
     return tokens
+
+
+def tp_exchange_bytes(world: int, max_rows: int, hidden: int) -> int:
+    return int(_lib_().aacc_tp_exchange_bytes(world, max_rows, hidden))
+
+
+def peer_buffer_alloc(nbytes: int) -> tuple[int, bytes]:
+    """Zero-filled dedicated device buffer + its 64-byte CUDA IPC handle (set-up only)."""
+    ptr = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(64)
+    _lib.check(_lib_().aacc_peer_buffer_alloc(nbytes, ctypes.byref(ptr), handle), "peer_buffer_alloc")
+    return ptr.value, handle.raw
+
+
+def peer_buffer_open(handle: bytes) -> int:
+    ptr = ctypes.c_void_p()
+    _lib.check(_lib_().aacc_peer_buffer_open(ctypes.create_string_buffer(handle, 64), ctypes.byref(ptr)),
+               "peer_buffer_open")
+    return ptr.value
+
+
+def peer_buffer_close(ptr: int) -> None:
+    _lib.check(_lib_().aacc_peer_buffer_close(ptr), "peer_buffer_close")
+
+
+def peer_buffer_free(ptr: int) -> None:
+    _lib.check(_lib_().aacc_peer_buffer_free(ptr), "peer_buffer_free")
+
+
+def tp_allreduce_add_rmsnorm(src, splits: int, buffers, rank: int, max_rows: int, residual, w, eps: float, out,
+                             two_shot: bool = False):
+    """All-reduce of a RowParallel output over the group's exchange buffers, fused with the
+    split-K sum (src fp32 [splits, M, H], or bf16 [M, H] with splits=0), the residual add
+    (residual updated in place) and the RMSNorm into `out`."""
+    M, H = residual.shape
+    world = len(buffers)
+    arr = (ctypes.c_void_p * world)(*buffers)
+    _lib.check(_lib_().aacc_tp_allreduce_add_rmsnorm(_p(src), splits, arr, world, rank, int(two_shot), max_rows,
+                                                     _p(residual), _p(w), _p(out), M, H, eps, _stream()),
+               "tp_allreduce_add_rmsnorm")
+    return out

@@ -22,7 +22,7 @@ import torch.nn as nn
 
 from ..kv_cache import PagedKVCache
 from ..runtime import LayerWeights, Qwen3Runtime, TPComm, interleave_gate_up, rope_table
-from .distributed import (get_tp_group, get_tp_rank, get_tp_world_size, split_tensor_along_dim,
+from .distributed import (get_tp_cpu_group, get_tp_group, get_tp_rank, get_tp_world_size, split_tensor_along_dim,
                           tensor_model_parallel_all_gather)
 from .model import Qwen3Config, RMSNorm, RotaryEmbedding
 from .parallel_layers import ColumnParallelLinear, QKVParallelLinear, RowParallelLinear, qkv_rank_rows
@@ -152,7 +152,7 @@ class Qwen3ForCausalLMTP(nn.Module):
                                    l.self_attn.q_norm.weight.data, l.self_attn.k_norm.weight.data,
                                    l.self_attn.o_proj.weight.data, l.post_attention_layernorm.weight.data,
                                    l.mlp._gate_up, l.mlp.down_proj.weight.data) for l in self.model.layers]
-            comm = TPComm(self.tp_rank, self.tp_size, get_tp_group())
+            comm = TPComm(self.tp_rank, self.tp_size, get_tp_group(), get_tp_cpu_group())
             self.runtime = Qwen3Runtime(
                 hidden=cfg.hidden_size, intermediate=cfg.intermediate_size, num_q_heads=cfg.num_attention_heads,
                 num_kv_heads=cfg.num_key_value_heads, vocab=cfg.vocab_size, eps=cfg.rms_norm_eps, layers=layers,

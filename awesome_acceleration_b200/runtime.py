@@ -30,6 +30,7 @@ kernels.
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -77,11 +78,60 @@ def rope_table(max_pos: int, head_dim: int, theta: float, device, dtype=torch.bf
     return torch.cat([emb.cos().to(dtype)[:, :half], emb.sin().to(dtype)[:, :half]], dim=-1).contiguous()
 
 
+class PeerExchange:
+    """NVLink exchange buffers of one TP group for aacc_tp_allreduce_add_rmsnorm.
+
+    Every rank allocates one dedicated, zero-filled device buffer and maps
+    every peer's through CUDA IPC; the handles travel over the group's Gloo
+    twin.  All ranks construct it together (it is collective) and only when
+    every rank can reach every other rank's GPU peer-to-peer; otherwise
+    ``create`` returns None on all ranks and the NCCL path stays in use.
+    """
+
+    def __init__(self, rank: int, world: int, cpu_group, max_rows: int, hidden: int, two_shot: bool):
+        self.rank, self.world, self.max_rows, self.hidden, self.two_shot = rank, world, max_rows, hidden, two_shot
+        self.cpu_group = cpu_group
+        self.own, handle = K.peer_buffer_alloc(K.tp_exchange_bytes(world, max_rows, hidden))
+        dev = torch.cuda.current_device()
+        info = [None] * world
+        torch.distributed.all_gather_object(info, (handle, dev), group=cpu_group)
+        ok = all(p == rank or torch.cuda.can_device_access_peer(dev, d) for p, (_, d) in enumerate(info))
+        oks = [None] * world
+        torch.distributed.all_gather_object(oks, ok, group=cpu_group)
+        self.ptrs: list[int] = []
+        self.usable = all(oks)
+        if self.usable:
+            self.ptrs = [self.own if p == rank else K.peer_buffer_open(h) for p, (h, _) in enumerate(info)]
+        torch.distributed.barrier(group=cpu_group)  # every buffer zeroed and mapped before the first push
+
+    @classmethod
+    def create(cls, rank, world, cpu_group, max_rows, hidden, two_shot):
+        ex = cls(rank, world, cpu_group, max_rows, hidden, two_shot)
+        if not ex.usable:
+            ex.close()
+            return None
+        return ex
+
+    def close(self) -> None:
+        """Collective: unmap the peers' buffers, wait for every rank, free our own."""
+        if self.own is None:
+            return
+        torch.cuda.synchronize()
+        for p, ptr in enumerate(self.ptrs):
+            if p != self.rank:
+                K.peer_buffer_close(ptr)
+        self.ptrs = []
+        torch.distributed.barrier(group=self.cpu_group)
+        K.peer_buffer_free(self.own)
+        self.own = None
+
+
 class TPComm:
     """Collective hooks of the tensor-parallel path (identity at TP=1)."""
 
-    def __init__(self, rank: int = 0, size: int = 1, group=None):
-        self.rank, self.size, self.group = rank, size, group
+    def __init__(self, rank: int = 0, size: int = 1, group=None, cpu_group=None):
+        self.rank, self.size, self.group, self.cpu_group = rank, size, group, cpu_group
+        self.exchange: PeerExchange | None = None
 
     def all_reduce(self, t: torch.Tensor) -> None:
         if self.size > 1:
@@ -90,6 +140,32 @@ class TPComm:
     def all_gather(self, out: torch.Tensor, t: torch.Tensor) -> None:
         """out [size, n] <- every rank's t [n] (rank order)."""
         torch.distributed.all_gather_into_tensor(out.view(-1), t, group=self.group)
+
+    def enable_peer_exchange(self, max_rows: int, hidden: int) -> None:
+        """Set up the NVLink exchange for RowParallel outputs of up to max_rows rows
+        (collective over the TP group).  AACC_TP_EXCHANGE=0 keeps NCCL;
+        AACC_TP_TWO_SHOT=0 selects the one-shot exchange (two-shot measured faster from 2 ranks up)."""
+        if (self.size < 2 or self.size > 8 or self.cpu_group is None or self.exchange is not None
+                or os.environ.get("AACC_TP_EXCHANGE", "1") == "0"
+                or torch.distributed.get_backend(self.group) != "nccl" or (hidden // 8) % self.size):
+            return
+        two_shot = os.environ.get("AACC_TP_TWO_SHOT", "1") != "0"
+        self.exchange = PeerExchange.create(self.rank, self.size, self.cpu_group, max_rows, hidden, two_shot)
+
+    def allreduce_add_rmsnorm(self, src, splits: int, res, w, eps: float, out) -> bool:
+        """res += all_reduce(src) (src: fp32 split-K partials, or bf16 with splits=0), out = rmsnorm(res)
+        in one NVLink kernel; False when the exchange is off or M exceeds its capacity."""
+        ex = self.exchange
+        if ex is None or res.shape[0] > ex.max_rows:
+            return False
+        K.tp_allreduce_add_rmsnorm(src, splits, ex.ptrs, self.rank, ex.max_rows, res, w, eps, out,
+                                   two_shot=ex.two_shot)
+        return True
+
+    def close(self) -> None:
+        if self.exchange is not None:
+            self.exchange.close()
+            self.exchange = None
 
 
 class _DecodeBuffers:
@@ -149,6 +225,9 @@ class Qwen3Runtime:
         self.d2h_bytes = 0
         self._pinned = torch.zeros((3, max_batch), dtype=torch.int64).pin_memory()
         self._tok_host = torch.zeros(max_batch, dtype=torch.int64).pin_memory()
+        # TP: RowParallel outputs of decode-sized batches go over NVLink peer memory
+        # (one fused kernel) instead of NCCL + separate residual/norm kernels.
+        self.comm.enable_peer_exchange(max_batch, hidden)
 
     # ------------------------------------------------------------------ layers
     def _splits(self, M, w, part):
@@ -196,9 +275,13 @@ class Qwen3Runtime:
             if self.comm.size == 1:
                 K.splitk_add_rmsnorm(pv, splits, res, norm_w, self.eps, out=x)
                 return
+            if self.comm.allreduce_add_rmsnorm(pv, splits, res, norm_w, self.eps, x):
+                return
             K.splitk_reduce(pv, splits, delta)
         else:
             K.gemm(inp, w, out=delta)
+            if self.comm.size > 1 and self.comm.allreduce_add_rmsnorm(delta, 0, res, norm_w, self.eps, x):
+                return
         self.comm.all_reduce(delta)
         K.add_rmsnorm(delta, res, norm_w, self.eps, out=x)
 

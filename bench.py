@@ -433,6 +433,8 @@ def run_cfg4(args, device):
     launches = lib.aacc_launch_count() - n0 + (rt.graph_replays - r0) * rt.graph_launches.get(n_seqs, 0)
     t_max = max_over_ranks(args, elapsed)
     value = dp * n_seqs * out * args.steps / t_max
+    ex = rt.comm.exchange
+    exchange = "none" if tp == 1 else "nccl" if ex is None else ("nvlink two-shot" if ex.two_shot else "nvlink one-shot")
     pk, kind = peaks()
     n_dec = out - 1
     kv_tok = 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * 128 * 2 // tp
@@ -451,7 +453,7 @@ def run_cfg4(args, device):
         "data": "synthetic (uniform random token ids, random-init weights)",
         "config": {"workload": "cfg4: Qwen3-8B TP" + (" [SMALL]" if args.small else ""), "global_batch": n_seqs * dp,
                    "seq_len": prompt + out, "parallelism": f"tp{tp}" + (f"xdp{dp}" if dp > 1 else ""),
-                   "l2": "inputs larger than L2"},
+                   "l2": "inputs larger than L2", "row_parallel_exchange": exchange},
         "gpu_launches": int(launches), "clocks": clk.summary(),
         "phases": {"prefill_ms": round(prefill_s / args.steps * 1e3, 1), "decode_ms": round(decode_s * 1e3, 1),
                    "decode_ms_per_step": round(decode_s / n_dec * 1e3, 3),

@@ -249,6 +249,43 @@ int aacc_argmax_rows(const void* logits, int64_t M, int64_t vocab, int64_t* toke
 int aacc_argmax_merge(const float* cand_val, const int64_t* cand_idx, int64_t M, int shards,
                       int64_t* tokens, cudaStream_t stream);
 
+/* ---- tensor-parallel exchange over NVLink peer memory -------------------- */
+
+/* Bytes of the exchange buffer each rank of a TP group allocates for
+ * aacc_tp_allreduce_add_rmsnorm (flags + double-buffered receive areas). */
+int64_t aacc_tp_exchange_bytes(int world, int64_t max_rows, int64_t hidden);
+
+/* Set-up only (the one place this library allocates device memory): a
+ * zero-filled cudaMalloc of `bytes` on the current device and its CUDA IPC
+ * handle (64 bytes written to ipc_handle).  A dedicated allocation, so that
+ * the handle maps exactly this buffer in the peers.  Replaces the NCCL
+ * communicator set-up of the reference's TP groups (model/distributed.py:39-95)
+ * for this one collective. */
+int aacc_peer_buffer_alloc(int64_t bytes, void** ptr, void* ipc_handle);
+/* Map a peer's buffer (its ipc_handle) into this process (P2P over NVLink). */
+int aacc_peer_buffer_open(const void* ipc_handle, void** ptr);
+int aacc_peer_buffer_close(void* peer_ptr);
+int aacc_peer_buffer_free(void* ptr);
+
+/* RowParallel all-reduce fused with the residual add and the next RMSNorm,
+ * over the group's exchange buffers (buffers[p] = rank p's buffer as mapped in
+ * this process, buffers[rank] = this rank's own):
+ *   delta_r  = bf16(sum_s partial[s])        (splits >= 1, fp32 [splits][M][hidden])
+ *            | src                            (splits == 0, bf16 [M][hidden])
+ *   delta    = bf16(sum over ranks of delta_r, fp32 in rank order)
+ *   residual = bf16(residual + delta); y = RMSNorm(residual) * w
+ * Every rank of the group must make the same sequence of calls with the same
+ * M (<= max_rows), world and two_shot, in stream order.  one-shot
+ * (two_shot = 0) pushes the whole output to every rank; two-shot
+ * reduce-scatters by columns and all-gathers the reduced slices.  A peer that
+ * does not arrive within 2 s sets the device error word (bit 64) and the
+ * output is invalid.  Replaces RowParallelLinear's dist.all_reduce
+ * (parallel_layers.py:190-195) plus the residual add and RMSNorm after it
+ * (model/model.py:259-265; model/model_tp.py:311-322). */
+int aacc_tp_allreduce_add_rmsnorm(const void* src, int splits, void* const* buffers, int world, int rank,
+                                  int two_shot, int64_t max_rows, void* residual, const void* w, void* y, int64_t M,
+                                  int64_t hidden, float eps, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

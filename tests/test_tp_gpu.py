@@ -160,3 +160,100 @@ def test_llmtp_engine_two_ranks(cuda):
     toks, gen = res[0]
     assert gen == [9] * 6
     assert all(len(t) == 9 for t in toks)
+
+
+def _exchange_case(rank, world):
+    """The NVLink exchange kernel against NCCL: all-gather every rank's bf16
+    output, sum in fp32 in rank order, round, then the add+RMSNorm kernel."""
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import torch.distributed as dist
+    from awesome_acceleration_b200 import _lib
+    from awesome_acceleration_b200 import kernels as K
+    from awesome_acceleration_b200.model import distributed as D
+    from awesome_acceleration_b200.runtime import TPComm
+    D.init_distributed(world, timeout_s=120)
+    dev = torch.device("cuda", rank)
+    bad = []
+    for hidden in (1024, 4096):
+        comm = TPComm(rank, world, D.get_tp_group(), D.get_tp_cpu_group())
+        comm.enable_peer_exchange(256, hidden)
+        assert comm.exchange is not None
+        w = (1 + 0.1 * torch.randn(hidden, generator=torch.Generator().manual_seed(7))).bfloat16().to(dev)
+        step = 0
+        for two_shot in (False, True):
+            comm.exchange.two_shot = two_shot
+            for M, splits in ((1, 0), (37, 3), (128, 8), (256, 2), (200, 0)):
+                step += 1
+                g = torch.Generator().manual_seed(1000 * step + rank)
+                if splits:
+                    src = torch.randn(splits, M, hidden, generator=g).to(dev)
+                    mine = torch.empty(M, hidden, dtype=torch.bfloat16, device=dev)
+                    K.splitk_reduce(src, splits, mine)
+                else:
+                    src = torch.randn(M, hidden, generator=g).bfloat16().to(dev)
+                    mine = src.clone()
+                res0 = torch.randn(M, hidden, generator=torch.Generator().manual_seed(step)).bfloat16().to(dev)
+                # reference: exact fp32 sum in rank order of the all-gathered outputs
+                allv = torch.empty(world, M, hidden, dtype=torch.bfloat16, device=dev)
+                dist.all_gather_into_tensor(allv.view(-1), mine.view(-1), group=D.get_tp_group())
+                acc = torch.zeros(M, hidden, dtype=torch.float32, device=dev)
+                for p in range(world):
+                    acc += allv[p].float()
+                delta = acc.bfloat16()
+                res_ref, y_ref = res0.clone(), torch.empty_like(res0)
+                K.add_rmsnorm(delta, res_ref, w, 1e-6, out=y_ref)
+                if world == 2:  # NCCL's bf16 sum of two ranks is the same rounding
+                    nc = mine.clone()
+                    dist.all_reduce(nc, group=D.get_tp_group())
+                    if not torch.equal(nc, delta):
+                        bad.append(("nccl", hidden, two_shot, M, splits))
+                res, y = res0.clone(), torch.empty_like(res0)
+                assert comm.allreduce_add_rmsnorm(src, splits, res, w, 1e-6, y)
+                torch.cuda.synchronize()
+                if not (torch.equal(res, res_ref) and torch.equal(y, y_ref)):
+                    bad.append((hidden, two_shot, M, splits, (res.float() - res_ref.float()).abs().max().item(),
+                                (y.float() - y_ref.float()).abs().max().item()))
+        # graph replays keep the ranks' call counters in step
+        M = 64
+        src = torch.zeros(4, M, hidden, device=dev)
+        res, y = torch.zeros(M, hidden, dtype=torch.bfloat16, device=dev), torch.empty(M, hidden, dtype=torch.bfloat16,
+                                                                                     device=dev)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(graph, stream=s):
+                comm.allreduce_add_rmsnorm(src, 4, res, w, 1e-6, y)
+        torch.cuda.current_stream().wait_stream(s)
+        for it in range(5):
+            g = torch.Generator().manual_seed(50 + it + 100 * rank)
+            src.copy_(torch.randn(4, M, hidden, generator=g))
+            res.copy_(torch.randn(M, hidden, generator=torch.Generator().manual_seed(it)).bfloat16())
+            res0 = res.clone()
+            graph.replay()
+            torch.cuda.synchronize()
+            mine = torch.empty(M, hidden, dtype=torch.bfloat16, device=dev)
+            K.splitk_reduce(src, 4, mine)
+            allv = torch.empty(world, M, hidden, dtype=torch.bfloat16, device=dev)
+            dist.all_gather_into_tensor(allv.view(-1), mine.view(-1), group=D.get_tp_group())
+            acc = torch.zeros(M, hidden, dtype=torch.float32, device=dev)
+            for p in range(world):
+                acc += allv[p].float()
+            res_ref, y_ref = res0.clone(), torch.empty_like(res0)
+            K.add_rmsnorm(acc.bfloat16(), res_ref, w, 1e-6, out=y_ref)
+            if not (torch.equal(res, res_ref) and torch.equal(y, y_ref)):
+                bad.append(("graph", hidden, it))
+        del graph
+        assert _lib.device_error() == 0
+        comm.close()
+    return bad
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_exchange_kernel(cuda, world):
+    if _ngpu() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res = run_ranks(world, _exchange_case)
+    for r in range(world):
+        assert res[r] == [], f"rank {r}: {res[r]}"
