@@ -56,7 +56,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
   const int64_t b = blockIdx.z;
   const int Hq = Hkv * G;
   const int64_t row = rows[b];
-  int64_t ctx = (int64_t)seqlens[row] + ctx_add;
+  int64_t ctx = row < 0 ? 0 : (int64_t)seqlens[row] + ctx_add;  // negative rows are padding
   if (ctx > max_ctx) {  // max_ctx <= max_blocks * bs and <= max_splits * split_tokens
     if (threadIdx.x == 0 && s == 0) report(err, ERR_CTX_OOB);
     ctx = max_ctx;

@@ -44,6 +44,10 @@ __global__ void decode_slot_mapping_kernel(const int64_t* __restrict__ rows, con
   int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   int64_t row = rows[b];
+  if (row < 0) {  // padding row of a bucketed batch: no cache slot
+    out[b] = -1;
+    return;
+  }
   int64_t n = seqlens[row];
   int64_t j = n / bs;
   if (j >= max_blocks) {
@@ -65,7 +69,7 @@ __global__ void advance_seqlens_kernel(const int64_t* __restrict__ rows, int32_t
   griddep_wait();
   griddep_launch();
   int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (b < B) {
+  if (b < B && rows[b] >= 0) {  // negative rows are padding
     atomicAdd(&seqlens[rows[b]], 1);
     if (positions) positions[b] += 1;
   }

@@ -50,11 +50,18 @@ class _Request:
 
 
 def kv_sized_max_seqs(config: Qwen3Config, max_num_seqs: int, max_seq_len: int, reserve_gb: float,
-                      device, tp_size: int = 1) -> int:
-    """The reference's batch sizing from GPU memory (llm.py:58-71, llm_tp.py:160-178)."""
-    gpu_gb = torch.cuda.get_device_properties(device).total_memory / (1024 ** 3)
+                      device, tp_size: int = 1, prefill_chunk_tokens: int = 0) -> int:
+    """The reference's batch sizing from GPU memory (llm.py:58-71, llm_tp.py:160-178):
+    KV bytes per token (this rank's heads) against the memory left after a fixed
+    reserve.  Called once the weights are on the device, it also keeps the
+    memory they already hold and one prefill chunk's activations out of the
+    KV budget: the reference's fixed reserve only covers a 0.6B model."""
+    free, total = torch.cuda.mem_get_info(device)
     per_tok = 2 * config.num_key_value_heads * config.head_dim * 2 * config.num_hidden_layers // tp_size
-    avail = (gpu_gb - reserve_gb) * (1024 ** 3)
+    q_cols = config.num_attention_heads * config.head_dim // tp_size
+    act = prefill_chunk_tokens * (3 * config.hidden_size + 2 * q_cols + config.intermediate_size // tp_size) * 2
+    reserve = reserve_gb * (1024 ** 3)
+    avail = min(total - reserve, free - reserve - act)
     return max(1, min(max_num_seqs, int(avail / per_tok) // max_seq_len))
 
 
@@ -84,7 +91,8 @@ class LLM:
         if model_path is not None and os.path.exists(os.path.join(model_path, "tokenizer_config.json")):
             from transformers import AutoTokenizer
             self.tokenizer = AutoTokenizer.from_pretrained(model_path, trust_remote_code=True)
-        self.max_num_seqs = kv_sized_max_seqs(self.config, max_num_seqs, max_seq_len, 3.0, self.device)
+        self.max_num_seqs = kv_sized_max_seqs(self.config, max_num_seqs, max_seq_len, 3.0, self.device,
+                                              prefill_chunk_tokens=prefill_chunk_tokens)
         self.model.eval()
         self.model.use_cuda_graphs = use_cuda_graphs
         self.model.prefill_chunk_tokens = prefill_chunk_tokens

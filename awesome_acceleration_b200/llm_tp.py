@@ -78,7 +78,12 @@ class LLMTP:
                 os.path.exists(os.path.join(model_path, "tokenizer_config.json")):
             from transformers import AutoTokenizer
             self.tokenizer = AutoTokenizer.from_pretrained(model_path, trust_remote_code=True)
-        self.max_num_seqs = kv_sized_max_seqs(self.config, max_num_seqs, max_seq_len, 15.0, self.device, self.tp_size)
+        self.max_num_seqs = kv_sized_max_seqs(self.config, max_num_seqs, max_seq_len, 15.0, self.device, self.tp_size,
+                                              prefill_chunk_tokens)
+        if self.tp_size > 1:  # free memory differs a little per GPU; the group must agree on slots and buckets
+            n = torch.tensor([self.max_num_seqs], dtype=torch.int64)
+            torch.distributed.all_reduce(n, op=torch.distributed.ReduceOp.MIN, group=D.get_tp_cpu_group())
+            self.max_num_seqs = int(n.item())
         self.model.eval()
         self.model.use_cuda_graphs = use_cuda_graphs
         self.model.prefill_chunk_tokens = prefill_chunk_tokens
@@ -111,7 +116,7 @@ class LLMTP:
         """Leader: one packed [3, B] NCCL broadcast of ids | positions | rows
         into every rank's decode buffers (llm_tp.py:301-338)."""
         rt = self.model._rt()
-        B = len(rows)
+        B = rt.padded_batch(len(rows))  # padding rows included
         if self.is_tp_leader:
             rt.load_decode_inputs(ids, positions, rows)
             self._bcast[:3 * B].view(3, B).copy_(rt.buf.meta[:, :B])

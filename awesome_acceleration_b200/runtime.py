@@ -221,6 +221,7 @@ class Qwen3Runtime:
         self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.graph_launches: dict[int, int] = {}  # kernels per replay of the batch-B graph
         self.graph_replays = 0
+        self.replayed_launches = 0  # kernels run by graph replays (sum over replays of the graph's launches)
         self.h2d_bytes = 0  # host->device bytes staged by this runtime
         self.d2h_bytes = 0
         self._pinned = torch.zeros((3, max_batch), dtype=torch.int64).pin_memory()
@@ -326,30 +327,54 @@ class Qwen3Runtime:
         self._argmax(b.x[:B], ids, b.best[:B], b.lm_ws, logits=logits, g_best=g_best, g_tok=g_tok)
         K.advance_seqlens(rows, kv.seqlens, pos)
 
+    def padded_batch(self, B: int) -> int:
+        """Rows a decode step of B sequences runs: with CUDA graphs, B rounded
+        up to a bucket (a power of two up to 8, a multiple of 8 up to 64, then
+        of 32; at most max_batch), so that a batch that shrinks as sequences
+        finish replays a few captured graphs instead of capturing one per
+        size.  Rows past B are padding (slot index -1): the kernels skip
+        their cache reads and writes and the host ignores their tokens."""
+        if not self.use_graphs or B <= 0:
+            return B
+        if B <= 8:
+            p = 1 << (B - 1).bit_length()
+        elif B <= 64:
+            p = (B + 7) // 8 * 8
+        else:
+            p = (B + 31) // 32 * 32
+        return min(p, self.max_batch)
+
     def load_decode_inputs(self, ids, positions, rows) -> None:
-        """Stage one decode batch (host sequences of ints) into the static buffers."""
+        """Stage one decode batch (host sequences of ints) into the static
+        buffers, padded to padded_batch(len(rows)) rows."""
         B = len(rows)
         if B > self.max_batch:
             raise ValueError(f"decode batch {B} exceeds max_batch {self.max_batch}")
+        Bp = self.padded_batch(B)
         # The pinned staging buffer may still feed an in-flight copy.
         torch.cuda.current_stream().synchronize()
         p = self._pinned
         p[0, :B] = torch.as_tensor(ids, dtype=torch.int64)
         p[1, :B] = torch.as_tensor(positions, dtype=torch.int64)
         p[2, :B] = torch.as_tensor(rows, dtype=torch.int64)
-        self.buf.meta[:, :B].copy_(p[:, :B], non_blocking=True)
-        self.h2d_bytes += 3 * B * 8
+        p[:2, B:Bp] = 0
+        p[2, B:Bp] = -1
+        self.buf.meta[:, :Bp].copy_(p[:, :Bp], non_blocking=True)
+        self.h2d_bytes += 3 * Bp * 8
 
     def load_positions_rows(self, positions, rows) -> None:
         """Stage positions and rows only; the ids are already on the device
         (e.g. the prefill's next tokens copied into buf.ids)."""
         B = len(rows)
+        Bp = self.padded_batch(B)
         torch.cuda.current_stream().synchronize()
         p = self._pinned
         p[1, :B] = torch.as_tensor(positions, dtype=torch.int64)
         p[2, :B] = torch.as_tensor(rows, dtype=torch.int64)
-        self.buf.meta[1:, :B].copy_(p[1:, :B], non_blocking=True)
-        self.h2d_bytes += 2 * B * 8
+        p[1, B:Bp] = 0
+        p[2, B:Bp] = -1
+        self.buf.meta[1:, :Bp].copy_(p[1:, :Bp], non_blocking=True)
+        self.h2d_bytes += 2 * Bp * 8
 
     def reserve_decode(self, rows) -> None:
         """Host block bookkeeping for one decode step of `rows` (new token at lengths[row])."""
@@ -366,14 +391,35 @@ class Qwen3Runtime:
         if logits is not None or not self.use_graphs:
             self._decode_body(B, logits)
         else:
-            g = self._graphs.get(B)
+            Bp = self.padded_batch(B)
+            g = self._graphs.get(Bp)
             if g is None:
-                g = self._capture(B)
+                g = self._capture(Bp)
             g.replay()
             self.graph_replays += 1
+            self.replayed_launches += self.graph_launches[Bp]
         for r in rows:
             self.kv.lengths[r] += 1
         return self.buf.ids[:B]
+
+    def capture_buckets(self, max_rows: int | None = None) -> None:
+        """Capture the decode graph of every batch bucket up to max_rows ahead
+        of a run, so that none is captured while the batch shrinks.  Each
+        capture runs one eager step on all-padding rows, which reads and
+        writes no sequence state.  Collective under TP: every rank captures
+        the same sizes in the same order."""
+        if not self.use_graphs:
+            return
+        top = min(max_rows or self.max_batch, self.max_batch)
+        sizes = sorted({self.padded_batch(b) for b in range(1, top + 1)})
+        meta = self.buf.meta
+        saved = meta.clone()
+        meta[:2].zero_()
+        meta[2].fill_(-1)
+        for Bp in sizes:
+            if Bp not in self._graphs:
+                self._capture(Bp)
+        meta.copy_(saved)
 
     def _capture(self, B: int) -> torch.cuda.CUDAGraph:
         # Capturing must not change state: run the body once eagerly on a

@@ -462,6 +462,86 @@ def run_cfg4(args, device):
     }
 
 
+# --------------------------------------------------------------------------- cfg5: Qwen3-32B DP x TP
+def run_cfg5(args, device):
+    """Qwen3-32B architecture (random-init bf16), 512
+    requests with prompts ~U[256,4096] and outputs ~U[128,1024] (one request
+    per sequence with its own max_tokens), greedy, ignore_eos, through the
+    engine's public API: the TP-group leader runs continuous batching, the
+    other ranks serve it, and the requests are dealt round-robin over the DP
+    replicas (benchmark_tp.py:288-292).  TP = --tp (default: the world).
+    The timed region is the whole job through LLMTP.generate_ids (host token
+    lists in, host results out), so `value` is already end to end."""
+    from awesome_acceleration_b200 import _lib
+    from awesome_acceleration_b200.llm_tp import LLMTP
+    from awesome_acceleration_b200.model.model import Qwen3Config
+    tp = args.tp or args.world
+    cfg = Qwen3Config(hidden_size=5120, intermediate_size=25600, num_hidden_layers=64, num_attention_heads=64,
+                      num_key_value_heads=8, tie_word_embeddings=False)
+    n_req = 64 if args.small else 512
+    plo, phi, olo, ohi = (256, 1024, 32, 128) if args.small else (256, 4096, 128, 1024)
+    rng = np.random.default_rng(2025)
+    plen = rng.integers(plo, phi + 1, n_req)
+    olen = rng.integers(olo, ohi + 1, n_req)
+    g = torch.Generator().manual_seed(77)
+    prompts = [torch.randint(0, cfg.vocab_size, (int(n),), generator=g).tolist() for n in plen]
+    llm = LLMTP(None, max_num_seqs=n_req, max_seq_len=phi + ohi + 16, enable_tp=args.world > 1, tp_size=tp,
+                config=cfg, seed=7)
+    dp = llm.dp_size
+    mine = list(range(llm.dp_rank, n_req, dp))
+    rt = llm.model._rt()
+    rt.capture_buckets(min(len(mine), llm.max_num_seqs))
+    lib = _lib.load()
+    elapsed, gen = 0.0, 0
+    if llm.is_tp_leader:
+        for w in range(args.warmup):  # short jobs: scheduler, prefill and decode paths warm
+            futs = [llm.generate_ids([prompts[i][:64]], max_tokens=4 + w, ignore_eos=True) for i in mine[:8]]
+            [f.result() for f in futs]
+        torch.cuda.synchronize()
+        h2d0, d2h0, n0, r0, l0 = (rt.h2d_bytes, rt.d2h_bytes, lib.aacc_launch_count(), rt.graph_replays,
+                                  rt.replayed_launches)
+        with ClockSampler(torch.cuda.current_device()) as clk:
+            for _ in range(args.steps):
+                t0 = time.perf_counter()
+                futs = [llm.generate_ids([prompts[i]], max_tokens=int(olen[i]), ignore_eos=True) for i in mine]
+                outs = [f.result()[0] for f in futs]
+                torch.cuda.synchronize()
+                elapsed += time.perf_counter() - t0
+                gen += sum(o.generated_tokens for o in outs)
+        assert gen == args.steps * int(olen[mine].sum()), gen
+        h2d, d2h = rt.h2d_bytes - h2d0, rt.d2h_bytes - d2h0
+        replays = rt.graph_replays - r0
+        launches = lib.aacc_launch_count() - n0 + rt.replayed_launches - l0
+        clocks = clk.summary()
+        llm.stop()
+    else:
+        llm.serve_worker()
+        h2d = d2h = launches = replays = 0
+        clocks = {}
+    _lib.raise_on_device_error("cfg5 job")
+    t_max = max_over_ranks(args, elapsed)
+    total = torch.tensor([gen], dtype=torch.float64, device="cuda")
+    if args.world > 1:
+        torch.distributed.all_reduce(total)
+    value = float(total.item()) / t_max
+    return {
+        "metric": f"output tok/s (Qwen3-32B, {n_req} requests, prompts U[{plo},{phi}], outputs U[{olo},{ohi}], "
+                  f"greedy, TP{tp} x DP{dp})",
+        "value": round(value, 1), "unit": "output tok/s", "n_gpus": args.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(t_max / args.steps * 1e3, 1), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (uniform random token ids and lengths, random-init weights)",
+        "config": {"workload": "cfg5: Qwen3-32B DP x TP, continuous batching" + (" [SMALL]" if args.small else ""),
+                   "global_batch": n_req, "seq_len": phi + ohi, "parallelism": f"tp{tp}" + (f"xdp{dp}" if dp > 1 else ""),
+                   "max_num_seqs_per_replica": llm.max_num_seqs, "l2": "inputs larger than L2",
+                   "timing": "wall clock around LLMTP.generate_ids on each TP leader, max over ranks"},
+        "e2e": {"value": round(value, 1), "unit": "output tok/s", "h2d_bytes_per_step": int(h2d // args.steps),
+                "d2h_bytes_per_step": int(d2h // args.steps), "api": "LLMTP.generate_ids",
+                "note": "value is itself measured through the public API"},
+        "gpu_launches": int(launches), "clocks": clocks, "decode_steps": int(replays),
+    }
+
+
 # --------------------------------------------------------------------------- prefill GEMMs (tensor pipe)
 def run_gemm(args, device):
     """The four cfg2 projections on one prefill chunk (M tokens) or, with
@@ -574,8 +654,8 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg4", "attn", "gemm"])
-    ap.add_argument("--tp", type=int, default=0, help="cfg4: tensor-parallel size (default: the whole world)")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg4", "cfg5", "attn", "gemm"])
+    ap.add_argument("--tp", type=int, default=0, help="cfg4/cfg5: tensor-parallel size (default: the whole world)")
     ap.add_argument("--small", action="store_true", help="small case for profiler captures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--decode", action="store_true", help="gemm workload: decode-batch shapes")
@@ -598,7 +678,8 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                              device_id=device)
     try:
-        line = {"attn": run_attn, "gemm": run_gemm, "cfg2": run_cfg2, "cfg4": run_cfg4}[args.workload](args, device)
+        line = {"attn": run_attn, "gemm": run_gemm, "cfg2": run_cfg2, "cfg4": run_cfg4,
+                "cfg5": run_cfg5}[args.workload](args, device)
         if args.rank == 0 and args.workload == "cfg2" and not (args.no_cpu_baseline or args.profile):
             v, info = cpu_sample()
             line["cpu_baseline"] = {"value": round(v, 3), "unit": "output tok/s", "cores": info["cores"],

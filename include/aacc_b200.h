@@ -59,8 +59,9 @@ int aacc_kv_store(const void* k, const void* v, int64_t num_tokens, int64_t k_ro
 
 /* Flat cache slot of the next token of each decode row:
  * out[b] = block_tables[row][n / bs] * bs + n % bs, n = seqlens[row],
- * row = slot_indices[b].  (The position the reference writes at,
- * cache_seqlens[slot], model/model.py:233-238.) */
+ * row = slot_indices[b]; a negative row is padding and gets -1 (no store).
+ * (The position the reference writes at, cache_seqlens[slot],
+ * model/model.py:233-238.) */
 int aacc_decode_slot_mapping(const int64_t* slot_indices, const int32_t* seqlens,
                              const int32_t* block_tables, int64_t max_blocks, int block_size,
                              int64_t num_blocks, int64_t* slot_mapping_out, int64_t batch,
@@ -69,7 +70,8 @@ int aacc_decode_slot_mapping(const int64_t* slot_indices, const int32_t* seqlens
 /* seqlens[slot_indices[b]] += 1 for b < batch
  * (model/model.py:241 `_cache_seqlens[slot_indices] += 1`); when positions
  * is not NULL also positions[b] += 1 (the scheduler's `pos += 1`,
- * llm.py:419), so a decode step can be replayed on device. */
+ * llm.py:419), so a decode step can be replayed on device.  Padding rows
+ * (negative slot index) are left alone. */
 int aacc_advance_seqlens(const int64_t* slot_indices, int32_t* seqlens, int64_t* positions, int64_t batch,
                          cudaStream_t stream);
 
@@ -88,7 +90,8 @@ int64_t aacc_paged_decode_workspace_bytes(int64_t batch, int num_q_heads, int64_
                                           int split_tokens);
 
 /* Decode attention of one query token per row over its paged context of
- * seqlens[row] + ctx_add tokens (GQA, softmax scale `scale`, non-causal).
+ * seqlens[row] + ctx_add tokens (GQA, softmax scale `scale`, non-causal);
+ * a padding row (negative slot index) reads nothing and outputs zeros.
  * q, out: [batch][num_q_heads][128].  split_tokens (multiple of 64, 0 =
  * default) is the context length one CTA streams; longer contexts are split
  * and merged.  Replaces flash_attn_with_kvcache (model/model.py:233-240,

@@ -136,3 +136,27 @@ def test_export_import_request_kv(cuda):
             seq.append(rt.read_tokens(1)[0])
         outs.append(seq)
     assert outs[0] == outs[1]
+
+
+def test_bucketed_decode_graphs_match_eager(cuda):
+    """Per-request max_tokens make the decode batch shrink step by step; with
+    CUDA graphs the runtime pads it to a bucket (padding rows have slot -1)
+    and replays a few graphs.  Every stream must equal the eager run, which
+    uses the exact batch size."""
+    from awesome_acceleration_b200.llm import LLM
+    sd = init_weights(TINY, 44, norm_jitter=0.1)
+    lens = [60, 1, 13, 33, 2, 59, 20, 41, 7, 18, 50]
+    prompts = [p[:n] for p, n in zip(random_prompts(len(lens), 60, TINY.vocab_size, 45), lens)]
+    max_toks = [3, 17, 1, 9, 12, 5, 20, 2, 14, 8, 11]
+    runs = []
+    for graphs in (False, True):
+        llm = LLM(model=_model(sd), max_num_seqs=10, max_seq_len=200, use_cuda_graphs=graphs)
+        futs = [llm.generate_ids([p], max_tokens=t, ignore_eos=True) for p, t in zip(prompts, max_toks)]
+        outs = [f.result(timeout=120)[0] for f in futs]
+        assert [o.generated_tokens for o in outs] == max_toks
+        runs.append([o.token_ids for o in outs])
+        rt = llm.model._rt()
+        if graphs:
+            assert set(rt._graphs) <= {1, 2, 4, 8, 10}, sorted(rt._graphs)  # 9-10 rows: capped at max_batch
+        llm.stop()
+    assert runs[0] == runs[1]
