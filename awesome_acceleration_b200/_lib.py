@@ -49,7 +49,9 @@ SIGNATURES: dict[str, tuple] = {
     "aacc_qkv_norm_rope_store": (I32, [P, P, P, P, F32, P, P, I64, P, P, P, P, I64, I32, I32, I32, I64, I64, P]),
     "aacc_lm_head_workspace_bytes": (I64, [I64, I64]),
     "aacc_lm_head_argmax": (I32, [P, P, I64, I64, I64, I64, P, P, P, P, I64, P]),
+    "aacc_lm_head_sample": (I32, [P, P, I64, I64, I64, I64, P, P, P, P, P, P, P, I64, P]),
     "aacc_argmax_rows": (I32, [P, I64, I64, P, P]),
+    "aacc_sample_rows": (I32, [P, I64, I64, P, P, P, P, P]),
     "aacc_argmax_merge": (I32, [P, P, I64, I32, P, P]),
     "aacc_tp_exchange_bytes": (I64, [I32, I64, I64]),
     "aacc_peer_buffer_alloc": (I32, [I64, P, P]),

@@ -16,13 +16,16 @@
 //   EPI_QKV     per-head RMSNorm (q_norm / k_norm) + RoPE for Q/K heads, then
 //               Q to q_out and K/V rows straight into the paged KV cache
 //   EPI_ARGMAX  per-row (max, first index) of bf16(acc) over each 128-column
-//               group (lm_head + greedy sampling without materialised logits)
+//               group (lm_head + greedy sampling without materialised logits);
+//               rows with a temperature > 0 take the max of
+//               bf16(acc / T) + Gumbel noise instead (temperature sampling)
 //
 // Decode batches (M <= 256) are weight-bandwidth bound: every weight byte is
 // read once (MT=2 keeps both 128-row halves of the batch in one CTA);
 // prefill tiles (MT=2, BN=256) are tensor-pipe bound.
 #include "common.cuh"
 #include "host.h"
+#include "sample.cuh"
 
 namespace aacc {
 
@@ -51,6 +54,10 @@ struct EpiParams {
   float* part_val;
   int32_t* part_idx;
   int64_t n_groups;
+  const float* temperature;  // per row, NULL = all greedy
+  const int64_t* seeds;      // per row
+  const int64_t* counters;   // per row (position of the sampled token's input)
+  int64_t vocab_offset;      // global id of column 0 (vocab-parallel shard)
   unsigned* err;
 };
 
@@ -262,18 +269,36 @@ __device__ __forceinline__ void epilogue_group(uint32_t tcol, int64_t m, bool ro
   } else {  // EPI_ARGMAX
     float best = -INFINITY;
     int32_t bi = 0x7fffffff;
+    float temp = 0.f;
+    uint64_t key = 0;
+    if (row_ok && p.temperature) {
+      temp = p.temperature[m];
+      if (temp > 0.f) key = sample_key(p.seeds[m], p.counters[m]);
+    }
 #pragma unroll 1
     for (int c = 0; c < 128; c += 16) {
       float v[16];
       tmem_ld16(tcol + c, v);
       if (row_ok) {
+        if (temp > 0.f) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int64_t n = n0 + c + i;
-          const float x = rbf(v[i]);
-          if (n < N && x > best) {
-            best = x;
-            bi = (int32_t)n;
+          for (int i = 0; i < 16; ++i) {
+            const int64_t n = n0 + c + i;
+            const float x = rbf(rbf(v[i]) / temp) + gumbel_noise(key, (uint32_t)(p.vocab_offset + n));
+            if (n < N && x > best) {
+              best = x;
+              bi = (int32_t)n;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int64_t n = n0 + c + i;
+            const float x = rbf(v[i]);
+            if (n < N && x > best) {
+              best = x;
+              bi = (int32_t)n;
+            }
           }
         }
         if (p.out) {
@@ -592,7 +617,16 @@ int64_t aacc_lm_head_workspace_bytes(int64_t M, int64_t vocab) {
 int aacc_lm_head_argmax(const void* x, const void* w, int64_t M, int64_t vocab, int64_t K, int64_t vocab_offset,
                         int64_t* tokens, float* best_val, void* logits, void* workspace, int64_t workspace_bytes,
                         cudaStream_t stream) {
+  return aacc_lm_head_sample(x, w, M, vocab, K, vocab_offset, nullptr, nullptr, nullptr, tokens, best_val, logits,
+                             workspace, workspace_bytes, stream);
+}
+
+int aacc_lm_head_sample(const void* x, const void* w, int64_t M, int64_t vocab, int64_t K, int64_t vocab_offset,
+                        const float* temperature, const int64_t* seeds, const int64_t* counters, int64_t* tokens,
+                        float* best_val, void* logits, void* workspace, int64_t workspace_bytes, cudaStream_t stream) {
   int st = gemm_check(x, w, M, vocab, K, "lm_head_argmax");
+  if (temperature && (!seeds || !counters))
+    return set_error(AACC_ERR_INVALID, "lm_head_sample: temperatures need seeds and counters");
   if (st || M == 0) return st;
   const int64_t groups = (vocab + 127) / 128;
   if (!workspace || workspace_bytes < aacc_lm_head_workspace_bytes(M, vocab))
@@ -605,6 +639,10 @@ int aacc_lm_head_argmax(const void* x, const void* w, int64_t M, int64_t vocab, 
   p.part_val = (float*)workspace;
   p.part_idx = (int32_t*)((float*)workspace + M * groups);
   p.n_groups = groups;
+  p.temperature = temperature;
+  p.seeds = seeds;
+  p.counters = counters;
+  p.vocab_offset = vocab_offset;
   p.err = device_error_ptr();
   st = gemm_dispatch<EPI_ARGMAX>(x, w, M, vocab, K, p, stream);
   if (st) return st;

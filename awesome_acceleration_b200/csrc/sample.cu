@@ -1,6 +1,8 @@
-// Greedy sampling over materialised logits and the vocab-parallel argmax merge.
+// Greedy and temperature sampling over materialised logits, and the
+// vocab-parallel argmax merge.
 #include "common.cuh"
 #include "host.h"
+#include "sample.cuh"
 
 namespace aacc {
 
@@ -43,6 +45,27 @@ __global__ void argmax_rows_kernel(const bf16* __restrict__ logits, int64_t voca
   if (threadIdx.x == 0) tokens[m] = bi == INT64_MAX ? 0 : bi;
 }
 
+// Temperature sampling over materialised bf16 logits: the same Gumbel-max
+// draw (and noise) as the lm_head epilogue; rows with T <= 0 stay greedy.
+__global__ void sample_rows_kernel(const bf16* __restrict__ logits, int64_t vocab, const float* __restrict__ temp,
+                                   const int64_t* __restrict__ seeds, const int64_t* __restrict__ counters,
+                                   int64_t* __restrict__ tokens) {
+  griddep_wait();
+  griddep_launch();
+  const int64_t m = blockIdx.x;
+  const float t = temp[m];
+  const uint64_t key = sample_key(seeds[m], counters[m]);
+  float bv = -INFINITY;
+  int64_t bi = INT64_MAX;
+  const bf16* row = logits + m * vocab;
+  for (int64_t n = threadIdx.x; n < vocab; n += blockDim.x) {
+    const float x = bf(row[n]);
+    better(bv, bi, t > 0.f ? rbf(x / t) + gumbel_noise(key, (uint32_t)n) : x, n);
+  }
+  block_argmax(bv, bi);
+  if (threadIdx.x == 0) tokens[m] = bi == INT64_MAX ? 0 : bi;
+}
+
 __global__ void argmax_merge_kernel(const float* __restrict__ cv, const int64_t* __restrict__ ci, int shards,
                                     int64_t* __restrict__ tokens) {
   griddep_wait();
@@ -67,6 +90,15 @@ int aacc_argmax_rows(const void* logits, int64_t M, int64_t vocab, int64_t* toke
   if (M == 0) return AACC_OK;
   return check_launch("argmax_rows", launch_k(argmax_rows_kernel, dim3((unsigned)M), dim3(512), 0, stream,
                                               (const bf16*)logits, vocab, tokens));
+}
+
+int aacc_sample_rows(const void* logits, int64_t M, int64_t vocab, const float* temperature, const int64_t* seeds,
+                     const int64_t* counters, int64_t* tokens, cudaStream_t stream) {
+  if (M < 0 || vocab <= 0 || (M > 0 && (!temperature || !seeds || !counters)))
+    return set_error(AACC_ERR_INVALID, "sample_rows: bad sizes or missing temperature/seeds/counters");
+  if (M == 0) return AACC_OK;
+  return check_launch("sample_rows", launch_k(sample_rows_kernel, dim3((unsigned)M), dim3(512), 0, stream,
+                                              (const bf16*)logits, vocab, temperature, seeds, counters, tokens));
 }
 
 int aacc_argmax_merge(const float* cand_val, const int64_t* cand_idx, int64_t M, int shards, int64_t* tokens,

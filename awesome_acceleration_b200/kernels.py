@@ -215,12 +215,21 @@ def lm_head_workspace_bytes(M: int, vocab: int) -> int:
     return int(_lib_().aacc_lm_head_workspace_bytes(M, vocab))
 
 
-def lm_head_argmax(x, w, tokens, workspace, *, logits=None, best_val=None, vocab_offset: int = 0):
+def lm_head_argmax(x, w, tokens, workspace, *, logits=None, best_val=None, vocab_offset: int = 0,
+                   temperature=None, seeds=None, counters=None):
+    """Next token of each row of x: greedy, or, for rows whose `temperature`
+    (fp32 [M]) is > 0, a sample of softmax(bf16(logits / T)) drawn with
+    counter-based Gumbel noise keyed by seeds / counters (int64 [M])."""
     M, K = x.shape
     V = w.shape[0]
-    _lib.check(_lib_().aacc_lm_head_argmax(
-        _p(x), _p(w), M, V, K, vocab_offset, _p(tokens), _p(best_val), _p(logits), _p(workspace),
-        workspace.numel() * workspace.element_size(), _stream()), "lm_head_argmax")
+    if temperature is not None:
+        for t, dt, name in ((temperature, torch.float32, "temperature"), (seeds, torch.int64, "seeds"),
+                            (counters, torch.int64, "counters")):
+            if t is None or t.dtype != dt or t.numel() < M or not t.is_contiguous():
+                raise ValueError(f"lm_head_argmax: {name} must be a contiguous {dt} tensor of >= {M} rows")
+    _lib.check(_lib_().aacc_lm_head_sample(
+        _p(x), _p(w), M, V, K, vocab_offset, _p(temperature), _p(seeds), _p(counters), _p(tokens), _p(best_val),
+        _p(logits), _p(workspace), workspace.numel() * workspace.element_size(), _stream()), "lm_head_argmax")
     return tokens
 
 
@@ -229,6 +238,20 @@ def argmax_rows(logits, tokens=None):
     if tokens is None:
         tokens = torch.empty(M, dtype=torch.int64, device=logits.device)
     _lib.check(_lib_().aacc_argmax_rows(_p(logits), M, V, _p(tokens), _stream()), "argmax_rows")
+    return tokens
+
+
+def sample_rows(logits, temperatures, seeds, counters, tokens=None):
+    """Temperature sampling over materialised logits [M, V] (per-row host
+    temperatures / seeds / counters); rows with temperature 0 take the argmax."""
+    M, V = logits.shape
+    dev = logits.device
+    t = torch.as_tensor(temperatures, dtype=torch.float32).to(dev)
+    sc = torch.as_tensor([list(seeds), list(counters)], dtype=torch.int64).to(dev)
+    if tokens is None:
+        tokens = torch.empty(M, dtype=torch.int64, device=dev)
+    _lib.check(_lib_().aacc_sample_rows(_p(logits), M, V, _p(t), _p(sc[0]), _p(sc[1]), _p(tokens), _stream()),
+               "sample_rows")
     return tokens
 
 

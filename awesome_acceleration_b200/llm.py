@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import bisect
 import concurrent.futures
+import itertools
 import os
 import queue
 import threading
@@ -47,6 +48,19 @@ class _Request:
     future: concurrent.futures.Future
     results: list = field(default_factory=list)
     pending_indices: list = field(default_factory=list)
+    seeds: list = field(default_factory=list)  # per prompt: key of its sampling noise (temperature > 0)
+
+
+_M64 = (1 << 64) - 1
+
+
+def sampling_seed(base: int, serial: int, index: int) -> int:
+    """Seed of prompt `index` of the `serial`-th request of an engine seeded
+    with `base` (SplitMix64 output function; a non-negative int64)."""
+    z = (base * 0x100000001B3 + serial * 0x10001 + index + 0x9E3779B97F4A7C15) & _M64
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & _M64
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & _M64
+    return (z ^ (z >> 31)) & 0x7FFFFFFFFFFFFFFF
 
 
 def kv_sized_max_seqs(config: Qwen3Config, max_num_seqs: int, max_seq_len: int, reserve_gb: float,
@@ -99,6 +113,8 @@ class LLM:
         self.model.fuse_qkv()
         self.model.init_kv_cache(self.max_num_seqs, max_seq_len, self.device, dtype, block_size=block_size)
         self._request_queue: queue.Queue[_Request] = queue.Queue()
+        self._base_seed = int(seed)  # sampling noise: one stream per (request, prompt)
+        self._serials = itertools.count(1)
         self._loop_running = False
         self._loop_thread = None
         self._loop_error: BaseException | None = None
@@ -130,11 +146,16 @@ class LLM:
         return self.model(input_ids, positions, slot_indices)[:, 0, :]
 
     def _sample_tokens(self, logits: torch.Tensor, temperature: float) -> list[int]:
-        """Greedy sampling (llm.py:215-219) with the B200 argmax kernel."""
-        if temperature != 0:
-            raise NotImplementedError("only greedy decoding (temperature=0) runs on the B200 path")
-        from .kernels import argmax_rows
-        return argmax_rows(logits.contiguous()).tolist()
+        """Next tokens from materialised logits [B, V] (llm.py:215-219): greedy
+        at temperature 0, else softmax(logits / T) sampling with the kernel's
+        Gumbel-max draw (fresh seeds from the engine's stream)."""
+        from .kernels import argmax_rows, sample_rows
+        if temperature == 0:
+            return argmax_rows(logits.contiguous()).tolist()
+        B = logits.shape[0]
+        serial = next(self._serials)
+        seeds = [sampling_seed(self._base_seed, serial, i) for i in range(B)]
+        return sample_rows(logits.contiguous(), [float(temperature)] * B, seeds, [0] * B).tolist()
 
     def _ensure_loop(self):
         if self._loop_error is not None:
@@ -145,8 +166,8 @@ class LLM:
             self._loop_thread.start()
 
     def _submit(self, token_ids, max_tokens, temperature, ignore_eos) -> concurrent.futures.Future:
-        if temperature != 0:
-            raise NotImplementedError("only greedy decoding (temperature=0) runs on the B200 path")
+        if temperature < 0:
+            raise ValueError(f"temperature must be >= 0, got {temperature}")
         for t in token_ids:
             if len(t) == 0:
                 raise ValueError("empty prompt")
@@ -154,9 +175,11 @@ class LLM:
                 raise ValueError(f"prompt of {len(t)} tokens does not fit max_seq_len={self.max_seq_len}")
         self._ensure_loop()
         future = concurrent.futures.Future()
+        serial = next(self._serials)
         req = _Request(token_ids=[list(map(int, t)) for t in token_ids], max_tokens=max_tokens,
                        temperature=temperature, ignore_eos=ignore_eos, future=future,
-                       results=[None] * len(token_ids), pending_indices=list(range(len(token_ids))))
+                       results=[None] * len(token_ids), pending_indices=list(range(len(token_ids))),
+                       seeds=[sampling_seed(self._base_seed, serial, i) for i in range(len(token_ids))])
         self._request_queue.put(req)
         return future
 
@@ -261,7 +284,9 @@ class LLM:
                 t0 = time.perf_counter()
                 seqs = [r.token_ids[i] for r, i, _ in new_work]
                 slots = [s for _, _, s in new_work]
-                toks = rt.prefill(seqs, slots).tolist()
+                # per-request temperature (the reference applies the first request's to the whole batch)
+                toks = rt.prefill(seqs, slots, temperatures=[r.temperature for r, _, _ in new_work],
+                                  seeds=[r.seeds[i] for r, i, _ in new_work]).tolist()
                 rt.d2h_bytes += 8 * len(toks)
                 self.stats["prefill_s"] += time.perf_counter() - t0
                 self.stats["prefill_tokens"] += sum(len(s) for s in seqs)
@@ -280,7 +305,9 @@ class LLM:
             slots = list(active.keys())
             B = len(slots)
             if staged != slots:
-                rt.load_decode_inputs([active[s][2][-1] for s in slots], [active[s][3] for s in slots], slots)
+                rt.load_decode_inputs([active[s][2][-1] for s in slots], [active[s][3] for s in slots], slots,
+                                      temperatures=[active[s][0].temperature for s in slots],
+                                      seeds=[active[s][0].seeds[active[s][1]] for s in slots])
                 staged = slots
             t0 = time.perf_counter()
             rt.decode_step(slots)

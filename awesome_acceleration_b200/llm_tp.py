@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import bisect
 import concurrent.futures
+import itertools
 import os
 import queue
 import threading
@@ -26,7 +27,7 @@ import time
 
 import torch
 
-from .llm import GenerationOutput, _Request, kv_sized_max_seqs
+from .llm import GenerationOutput, _Request, kv_sized_max_seqs, sampling_seed
 from .model import distributed as D
 from .model.model import Qwen3Config, Qwen3ForCausalLM
 from .model.model_tp import Qwen3ForCausalLMTP
@@ -89,7 +90,9 @@ class LLMTP:
         self.model.prefill_chunk_tokens = prefill_chunk_tokens
         self.model.fuse_qkv()
         self.model.init_kv_cache(self.max_num_seqs, max_seq_len, self.device, dtype, block_size=block_size)
-        self._bcast = torch.zeros(3 * self.model.max_batch, dtype=torch.int64, device=self.device)
+        self._bcast = torch.zeros(5 * self.model.max_batch, dtype=torch.int64, device=self.device)
+        self._base_seed = int(seed)  # sampling noise: one stream per (request, prompt)
+        self._serials = itertools.count(1)
         self._request_queue: queue.Queue | None = queue.Queue() if self.is_tp_leader else None
         self._loop_running = False
         self._loop_thread = None
@@ -112,17 +115,21 @@ class LLMTP:
         torch.cuda.synchronize(self.device)
         self.model.clear_all_slots()
 
-    def _stage_decode(self, ids, positions, rows):
-        """Leader: one packed [3, B] NCCL broadcast of ids | positions | rows
-        into every rank's decode buffers (llm_tp.py:301-338)."""
+    def _stage_decode(self, ids, positions, rows, temperatures=None, seeds=None):
+        """Leader: one packed [5, B] NCCL broadcast of ids | positions | rows |
+        sampling seeds | temperature bits into every rank's decode buffers
+        (llm_tp.py:301-338)."""
         rt = self.model._rt()
         B = rt.padded_batch(len(rows))  # padding rows included
+        bc = self._bcast[:5 * B].view(5, B)
         if self.is_tp_leader:
-            rt.load_decode_inputs(ids, positions, rows)
-            self._bcast[:3 * B].view(3, B).copy_(rt.buf.meta[:, :B])
-        D.broadcast_tensor(self._bcast[:3 * B], src=0)
+            rt.load_decode_inputs(ids, positions, rows, temperatures, seeds)
+            bc[:4].copy_(rt.buf.meta[:, :B])
+            bc[4].copy_(rt.buf.temp[:B].view(torch.int32))
+        D.broadcast_tensor(self._bcast[:5 * B], src=0)
         if not self.is_tp_leader:
-            rt.buf.meta[:, :B].copy_(self._bcast[:3 * B].view(3, B))
+            rt.buf.meta[:, :B].copy_(bc[:4])
+            rt.buf.temp[:B].view(torch.int32).copy_(bc[4])
 
     # ----------------------------------------------------------------- public API (leader)
     def generate(self, prompts: list[str], max_tokens: int = 100, temperature: float = 0.0,
@@ -140,8 +147,8 @@ class LLMTP:
     def generate_ids(self, token_ids: list[list[int]], max_tokens: int = 100, temperature: float = 0.0,
                      ignore_eos: bool = False) -> concurrent.futures.Future:
         assert self.is_tp_leader, "generate_ids() should only be called on the TP-group leader."
-        if temperature != 0:
-            raise NotImplementedError("only greedy decoding (temperature=0) runs on the B200 path")
+        if temperature < 0:
+            raise ValueError(f"temperature must be >= 0, got {temperature}")
         for t in token_ids:
             if len(t) == 0 or len(t) >= self.max_seq_len:
                 raise ValueError(f"prompt length {len(t)} outside [1, max_seq_len)")
@@ -152,8 +159,10 @@ class LLMTP:
             self._loop_thread = threading.Thread(target=self._inference_loop, daemon=True)
             self._loop_thread.start()
         fut = concurrent.futures.Future()
+        serial = next(self._serials)
         self._request_queue.put(_Request([list(map(int, t)) for t in token_ids], max_tokens, temperature, ignore_eos,
-                                         fut, [None] * len(token_ids), list(range(len(token_ids)))))
+                                         fut, [None] * len(token_ids), list(range(len(token_ids))),
+                                         [sampling_seed(self._base_seed, serial, i) for i in range(len(token_ids))]))
         return fut
 
     def chat(self, messages: list[dict], max_tokens: int = 100, temperature: float = 0.0,
@@ -196,7 +205,7 @@ class LLMTP:
             elif act == "clear_all_slots":
                 self.model.clear_all_slots()
             elif act == "prefill_flat":
-                rt.prefill(ctl["sequences"], ctl["slots"])
+                rt.prefill(ctl["sequences"], ctl["slots"], temperatures=ctl.get("temperatures"), seeds=ctl.get("seeds"))
             elif act == "decode":
                 if ctl.get("restage"):
                     rows = ctl["slots"]
@@ -271,8 +280,11 @@ class LLMTP:
             if new_work:
                 seqs = [r.token_ids[i] for r, i, _ in new_work]
                 slots = [s for _, _, s in new_work]
-                self._send({"action": "prefill_flat", "sequences": seqs, "slots": slots})
-                toks = rt.prefill(seqs, slots).tolist()
+                temps = [r.temperature for r, _, _ in new_work]  # per request (the reference uses the first's)
+                seeds = [r.seeds[i] for r, i, _ in new_work]
+                self._send({"action": "prefill_flat", "sequences": seqs, "slots": slots, "temperatures": temps,
+                            "seeds": seeds})
+                toks = rt.prefill(seqs, slots, temperatures=temps, seeds=seeds).tolist()
                 released = []
                 for (req, idx, slot), tok in zip(new_work, toks):
                     if 1 >= req.max_tokens or (not req.ignore_eos and tok == eos):
@@ -292,7 +304,9 @@ class LLMTP:
             restage = staged != slots
             self._send({"action": "decode", "batch_size": B, "restage": restage, "slots": slots if restage else None})
             if restage:
-                self._stage_decode([active[s][2][-1] for s in slots], [active[s][3] for s in slots], slots)
+                self._stage_decode([active[s][2][-1] for s in slots], [active[s][3] for s in slots], slots,
+                                   [active[s][0].temperature for s in slots],
+                                   [active[s][0].seeds[active[s][1]] for s in slots])
                 staged = slots
             rt.decode_step(slots)
             sampled = rt.read_tokens(B)

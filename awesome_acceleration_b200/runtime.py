@@ -172,8 +172,9 @@ class _DecodeBuffers:
     def __init__(self, B: int, H: int, Hq: int, I: int, vocab: int, tp: int, max_context: int, device):
         i64 = dict(dtype=torch.int64, device=device)
         bf = dict(dtype=torch.bfloat16, device=device)
-        self.meta = torch.zeros((3, B), **i64)  # ids | positions | rows
-        self.ids, self.pos, self.rows = self.meta[0], self.meta[1], self.meta[2]
+        self.meta = torch.zeros((4, B), **i64)  # ids | positions | rows | sampling seeds
+        self.ids, self.pos, self.rows, self.seed = self.meta[0], self.meta[1], self.meta[2], self.meta[3]
+        self.temp = torch.zeros(B, dtype=torch.float32, device=device)  # sampling temperature (0 = greedy)
         self.slot_map = torch.zeros(B, **i64)
         self.res = torch.zeros((B, H), **bf)
         self.x = torch.zeros((B, H), **bf)
@@ -224,7 +225,8 @@ class Qwen3Runtime:
         self.replayed_launches = 0  # kernels run by graph replays (sum over replays of the graph's launches)
         self.h2d_bytes = 0  # host->device bytes staged by this runtime
         self.d2h_bytes = 0
-        self._pinned = torch.zeros((3, max_batch), dtype=torch.int64).pin_memory()
+        self._pinned = torch.zeros((4, max_batch), dtype=torch.int64).pin_memory()
+        self._pinned_temp = torch.zeros(max_batch, dtype=torch.float32).pin_memory()
         self._tok_host = torch.zeros(max_batch, dtype=torch.int64).pin_memory()
         # TP: RowParallel outputs of decode-sized batches go over NVLink peer memory
         # (one fused kernel) instead of NCCL + separate residual/norm kernels.
@@ -298,10 +300,14 @@ class Qwen3Runtime:
             nxt = self.layers[i + 1].in_ln if i + 1 < L else self.final_norm
             self._row_parallel(act, lw.wd, delta, res, nxt, x, part)
 
-    def _argmax(self, x, tokens, best, ws, logits=None, g_best=None, g_tok=None):
-        """Greedy token of each row of x; under TP every rank scores its vocab
-        shard and the (value, id) candidates are all-gathered and merged."""
-        K.lm_head_argmax(x, self.lm_head, tokens, ws, logits=logits, best_val=best, vocab_offset=self.vocab_offset)
+    def _argmax(self, x, tokens, best, ws, logits=None, g_best=None, g_tok=None, sample=None):
+        """Next token of each row of x (greedy, or sampled for rows whose
+        temperature in `sample` = (temperature, seeds, counters) is > 0);
+        under TP every rank scores its vocab shard and the (score, id)
+        candidates are all-gathered and merged."""
+        t, sd, ct = sample if sample is not None else (None, None, None)
+        K.lm_head_argmax(x, self.lm_head, tokens, ws, logits=logits, best_val=best, vocab_offset=self.vocab_offset,
+                         temperature=t, seeds=sd, counters=ct)
         if self.comm.size > 1:
             self.comm.all_gather(g_best, best)
             self.comm.all_gather(g_tok, tokens)
@@ -324,7 +330,9 @@ class Qwen3Runtime:
         t = self.comm.size
         g_best = b.g_best[:t * B].view(t, B) if t > 1 else None
         g_tok = b.g_tok[:t * B].view(t, B) if t > 1 else None
-        self._argmax(b.x[:B], ids, b.best[:B], b.lm_ws, logits=logits, g_best=g_best, g_tok=g_tok)
+        # sampling counter = position of the input token (advances on device every step)
+        self._argmax(b.x[:B], ids, b.best[:B], b.lm_ws, logits=logits, g_best=g_best, g_tok=g_tok,
+                     sample=(b.temp[:B], b.seed[:B], pos))
         K.advance_seqlens(rows, kv.seqlens, pos)
 
     def padded_batch(self, B: int) -> int:
@@ -344,23 +352,28 @@ class Qwen3Runtime:
             p = (B + 31) // 32 * 32
         return min(p, self.max_batch)
 
-    def load_decode_inputs(self, ids, positions, rows) -> None:
+    def load_decode_inputs(self, ids, positions, rows, temperatures=None, seeds=None) -> None:
         """Stage one decode batch (host sequences of ints) into the static
-        buffers, padded to padded_batch(len(rows)) rows."""
+        buffers, padded to padded_batch(len(rows)) rows.  `temperatures` and
+        `seeds` (per row; default greedy) select temperature sampling."""
         B = len(rows)
         if B > self.max_batch:
             raise ValueError(f"decode batch {B} exceeds max_batch {self.max_batch}")
         Bp = self.padded_batch(B)
-        # The pinned staging buffer may still feed an in-flight copy.
+        # The pinned staging buffers may still feed an in-flight copy.
         torch.cuda.current_stream().synchronize()
-        p = self._pinned
+        p, pt = self._pinned, self._pinned_temp
         p[0, :B] = torch.as_tensor(ids, dtype=torch.int64)
         p[1, :B] = torch.as_tensor(positions, dtype=torch.int64)
         p[2, :B] = torch.as_tensor(rows, dtype=torch.int64)
-        p[:2, B:Bp] = 0
+        p[3, :B] = 0 if seeds is None else torch.as_tensor(seeds, dtype=torch.int64)
+        pt[:B] = 0.0 if temperatures is None else torch.as_tensor(temperatures, dtype=torch.float32)
+        p[:, B:Bp] = 0
         p[2, B:Bp] = -1
+        pt[B:Bp] = 0.0
         self.buf.meta[:, :Bp].copy_(p[:, :Bp], non_blocking=True)
-        self.h2d_bytes += 3 * Bp * 8
+        self.buf.temp[:Bp].copy_(pt[:Bp], non_blocking=True)
+        self.h2d_bytes += 4 * Bp * 8 + 4 * Bp
 
     def load_positions_rows(self, positions, rows) -> None:
         """Stage positions and rows only; the ids are already on the device
@@ -373,7 +386,8 @@ class Qwen3Runtime:
         p[2, :B] = torch.as_tensor(rows, dtype=torch.int64)
         p[1, B:Bp] = 0
         p[2, B:Bp] = -1
-        self.buf.meta[1:, :Bp].copy_(p[1:, :Bp], non_blocking=True)
+        self.buf.meta[1:3, :Bp].copy_(p[1:3, :Bp], non_blocking=True)
+        self.buf.temp[:Bp].zero_()  # greedy
         self.h2d_bytes += 2 * Bp * 8
 
     def reserve_decode(self, rows) -> None:
@@ -412,14 +426,16 @@ class Qwen3Runtime:
             return
         top = min(max_rows or self.max_batch, self.max_batch)
         sizes = sorted({self.padded_batch(b) for b in range(1, top + 1)})
-        meta = self.buf.meta
-        saved = meta.clone()
-        meta[:2].zero_()
+        meta, temp = self.buf.meta, self.buf.temp
+        saved, saved_t = meta.clone(), temp.clone()
+        meta.zero_()
         meta[2].fill_(-1)
+        temp.zero_()
         for Bp in sizes:
             if Bp not in self._graphs:
                 self._capture(Bp)
         meta.copy_(saved)
+        temp.copy_(saved_t)
 
     def _capture(self, B: int) -> torch.cuda.CUDAGraph:
         # Capturing must not change state: run the body once eagerly on a
@@ -456,12 +472,14 @@ class Qwen3Runtime:
 
     # ------------------------------------------------------------------ prefill
     def prefill(self, sequences: list[list[int]], rows: list[int], *, positions: list[list[int]] | None = None,
-                store_lengths: list[int] | None = None, all_logits: bool = False, last_logits: bool = False):
+                store_lengths: list[int] | None = None, all_logits: bool = False, last_logits: bool = False,
+                temperatures: list[float] | None = None, seeds: list[int] | None = None):
         """Packed (chunked) prefill of whole prompts into `rows`.
 
-        Returns the greedy next token of every sequence (device int64 [n]);
+        Returns the next token of every sequence (device int64 [n]): greedy,
+        or sampled where `temperatures` (per sequence, with `seeds`) is > 0;
         with ``last_logits`` also the bf16 logits of the last tokens [n, V];
-        with ``all_logits`` the logits of every token [T, V] instead."""
+        with ``all_logits`` the logits of every token [T, V] instead (greedy)."""
         kv = self.kv
         n = len(sequences)
         lens = [len(s) for s in sequences]
@@ -483,6 +501,14 @@ class Qwen3Runtime:
         self.h2d_bytes += host.numel() * 8
         ids_d, pos_d, smap_d = meta[0], meta[1], meta[2]
         tokens = torch.empty(n, dtype=torch.int64, device=dev)
+        samp = None
+        if temperatures is not None and any(t > 0 for t in temperatures):
+            last_pos = [L - 1 for L in lens] if positions is None else [int(p_[-1]) for p_ in positions]
+            sh = torch.tensor([list(seeds or [0] * n), last_pos], dtype=torch.int64).pin_memory()
+            th = torch.tensor(list(temperatures), dtype=torch.float32).pin_memory()
+            sd = sh.to(dev, non_blocking=True)
+            samp = (th.to(dev, non_blocking=True), sd[0], sd[1])  # counter = position of the last prompt token
+            self.h2d_bytes += sh.numel() * 8 + th.numel() * 4
         V = self.vocab if self.comm.size == 1 else self.vocab_local
         out_logits = None
         if all_logits:
@@ -553,12 +579,14 @@ class Qwen3Runtime:
                 a, m = ends[0][0], len(ends)
                 hx = K.gather_rows(xs, last_idx)
                 lg = out_logits[a:a + m] if last_logits else None
+                sm = None if samp is None else tuple(t[a:a + m] for t in samp)
                 if self.comm.size > 1:
                     gb = torch.empty((self.comm.size, m), dtype=torch.float32, device=dev)
                     gt = torch.empty((self.comm.size, m), dtype=torch.int64, device=dev)
-                    self._argmax(hx, tokens[a:a + m], best[a:a + m], lm_ws, logits=lg, g_best=gb, g_tok=gt)
+                    self._argmax(hx, tokens[a:a + m], best[a:a + m], lm_ws, logits=lg, g_best=gb, g_tok=gt,
+                                 sample=sm)
                 else:
-                    self._argmax(hx, tokens[a:a + m], best[a:a + m], lm_ws, logits=lg)
+                    self._argmax(hx, tokens[a:a + m], best[a:a + m], lm_ws, logits=lg, sample=sm)
         if all_logits:
             last = torch.from_numpy(offs[1:] - 1).to(dev)
             K.argmax_rows(K.gather_rows(out_logits, last), tokens)

@@ -241,6 +241,25 @@ int aacc_lm_head_argmax(const void* x, const void* w, int64_t M, int64_t vocab, 
                         int64_t vocab_offset, int64_t* tokens, float* best_val, void* logits,
                         void* workspace, int64_t workspace_bytes, cudaStream_t stream);
 
+/* aacc_lm_head_argmax with temperature sampling: row m with
+ * temperature[m] > 0 draws token ~ softmax(bf16(logits / T)) as
+ * argmax_v bf16(logit_v / T) + Gumbel(seeds[m], counters[m], global id v)
+ * (counter-based noise, the same on every TP rank; `counters` is the
+ * position of the token whose logits are sampled); best_val then holds the
+ * perturbed score, which the vocab-parallel merge compares.  Rows with
+ * temperature <= 0, or all rows when temperature is NULL, stay greedy.
+ * Replaces torch.multinomial(F.softmax(logits / temperature)) (llm.py:219,
+ * llm_tp.py:609-616). */
+int aacc_lm_head_sample(const void* x, const void* w, int64_t M, int64_t vocab, int64_t K, int64_t vocab_offset,
+                        const float* temperature, const int64_t* seeds, const int64_t* counters, int64_t* tokens,
+                        float* best_val, void* logits, void* workspace, int64_t workspace_bytes, cudaStream_t stream);
+
+/* Temperature sampling from materialised bf16 logits [M][vocab]: the draw of
+ * aacc_lm_head_sample (same noise for the same seed, counter and column) for
+ * rows with temperature > 0, argmax otherwise (llm.py:215-219). */
+int aacc_sample_rows(const void* logits, int64_t M, int64_t vocab, const float* temperature, const int64_t* seeds,
+                     const int64_t* counters, int64_t* tokens, cudaStream_t stream);
+
 /* Greedy sample from materialised bf16 logits [M][vocab] (llm.py:218). */
 int aacc_argmax_rows(const void* logits, int64_t M, int64_t vocab, int64_t* tokens,
                      cudaStream_t stream);

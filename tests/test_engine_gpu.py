@@ -62,8 +62,8 @@ def test_llm_stops_on_eos_and_max_seq_len(cuda):
     llm.config.eos_token_id = first
     out2 = llm.generate_ids([prompt], max_tokens=100, ignore_eos=False).result(timeout=60)[0]
     assert out2.token_ids == [first]
-    with pytest.raises(NotImplementedError):
-        llm.generate_ids([prompt], temperature=0.7)
+    with pytest.raises(ValueError):
+        llm.generate_ids([prompt], temperature=-0.7)
     with pytest.raises(ValueError):
         llm.generate_ids([[]])
     llm.stop()
@@ -160,3 +160,30 @@ def test_bucketed_decode_graphs_match_eager(cuda):
             assert set(rt._graphs) <= {1, 2, 4, 8, 10}, sorted(rt._graphs)  # 9-10 rows: capped at max_batch
         llm.stop()
     assert runs[0] == runs[1]
+
+
+def test_llm_temperature_sampling(cuda):
+    """temperature > 0 through the engine (llm.py:215-219): reproducible for a
+    given engine seed and request order, identical with and without CUDA
+    graphs, different from greedy and from another seed, and a
+    temperature-0 request in the same batch keeps its greedy stream."""
+    from awesome_acceleration_b200.llm import LLM
+    sd = init_weights(TINY, 46, norm_jitter=0.1)
+    prompts = [p[:n] for p, n in zip(random_prompts(4, 40, TINY.vocab_size, 47), [40, 9, 23, 31])]
+    runs = []
+    for graphs in (True, False, True):
+        llm = LLM(model=_model(sd), max_num_seqs=4, max_seq_len=128, seed=5, use_cuda_graphs=graphs)
+        hot = llm.generate_ids(prompts[:3], max_tokens=16, temperature=1.5, ignore_eos=True)
+        cold = llm.generate_ids(prompts[3:], max_tokens=16, temperature=0.0, ignore_eos=True)
+        runs.append(([o.token_ids for o in hot.result(timeout=120)], cold.result(timeout=120)[0].token_ids))
+        llm.stop()
+    assert runs[0] == runs[1] == runs[2]
+    llm = LLM(model=_model(sd), max_num_seqs=4, max_seq_len=128, seed=5)
+    greedy = llm.generate_ids(prompts, max_tokens=16, ignore_eos=True).result(timeout=120)
+    llm.stop()
+    other = LLM(model=_model(sd), max_num_seqs=4, max_seq_len=128, seed=6)
+    resampled = other.generate_ids(prompts[:3], max_tokens=16, temperature=1.5, ignore_eos=True).result(timeout=120)
+    other.stop()
+    assert runs[0][1] == greedy[3].token_ids
+    assert runs[0][0] != [o.token_ids for o in greedy[:3]]
+    assert runs[0][0] != [o.token_ids for o in resampled]

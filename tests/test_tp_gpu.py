@@ -150,7 +150,10 @@ def _llmtp_engine(rank, world):
         return None
     prompts = _prompts() + [[5, 6, 7], [9] * 20]  # more prompts than slots: continuous batching
     outs = llm.generate_ids(prompts, max_tokens=9, ignore_eos=True).result(timeout=240)
+    # temperature sampling across the TP group: the vocab shards' perturbed scores merge to one draw
+    hot = llm.generate_ids(prompts[:2], max_tokens=6, temperature=1.2, ignore_eos=True).result(timeout=240)
     llm.stop()
+    assert [len(o.token_ids) for o in hot] == [6, 6]
     return [o.token_ids for o in outs], [o.generated_tokens for o in outs]
 
 
