@@ -140,12 +140,16 @@ def gemm(x, w, out=None):
 def pick_splits(M: int, N: int, K: int, sms: int = 148, cap: int = 16, max_elems: int | None = None) -> int:
     """Largest divisor of K/64 (at most `cap`, and with splits*M*N fp32
     partials fitting `max_elems`) that keeps the split-K grid within one wave
-    of CTAs (one 128x128 tile per SM)."""
+    of CTAs (one 128x128 tile per SM) and whose fp32 partials (written, then
+    read back) are no more bytes than the weights (splits*M*N*4 <= N*K*2).
+    Measured on the cfg2 decode step (M=256): o_proj / down_proj at 4 splits
+    beat 8 by 1.0 / 0.6 us per layer; QKV keeps 2."""
     tiles = ((N + 127) // 128) * ((M + 127) // 128)
     nk = K // 64
     best = 1
     for d in range(1, min(nk, cap) + 1):
-        if nk % d == 0 and tiles * d <= sms and (max_elems is None or d * M * N <= max_elems):
+        if (nk % d == 0 and tiles * d <= sms and (max_elems is None or d * M * N <= max_elems)
+                and (d == 1 or 2 * d * M <= K)):
             best = d
     return best
 

@@ -128,6 +128,15 @@ def make_prompts(n, length, vocab, seed):
     return torch.randint(0, vocab, (n, length), generator=g).tolist()
 
 
+# DRAM bytes (read + write) per algorithmic byte of the decode attention, from
+# one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum of one launch
+# of `bench.py --workload attn --small`: 2.484 GB against 2.447 GB
+# algorithmic); the traffic of a full-size launch is scaled from it by the
+# bytes it must move (traffic grows in proportion to the context streamed).
+ATTN_TRAFFIC_PER_ALG_BYTE = 1.015
+ATTN_TRAFFIC_SOURCE = "ncu capture of --workload attn --small, scaled by algorithmic bytes"
+
+
 def attention_bytes(ctx, hq, hkv, bs):
     """Algorithmic bytes of one paged decode-attention launch."""
     ctx = np.asarray(ctx, dtype=np.int64)
@@ -315,9 +324,10 @@ def attention_roofline(llm, rows, reps=20):
     byts = attention_bytes(ctx, rt.Hq, rt.Hkv, kv.block_size)
     pk, kind = peaks()
     ach = byts / t / 1e9
-    return {"kernel": "paged_decode_kernel (+decode_combine_kernel)", "bound": "hbm",
+    return {"kernel": "paged_decode_kernel (split merge fused)", "bound": "hbm",
             "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(ach / pk["hbm_gbs"], 3),
-            "peak_kind": kind, "traffic": None, "bytes_per_launch": byts, "us_per_launch": round(t * 1e6, 2),
+            "peak_kind": kind, "traffic": int(byts * ATTN_TRAFFIC_PER_ALG_BYTE), "traffic_source": ATTN_TRAFFIC_SOURCE,
+            "bytes_per_launch": byts, "us_per_launch": round(t * 1e6, 2),
             "state": f"B={B}, ctx={min(ctx)}..{max(ctx)}"}
 
 
@@ -380,7 +390,8 @@ def run_attn(args, device):
             "config": {"workload": "cfg3 decode-attention microbenchmark", "pool_blocks": nb,
                        "l2": "flushed between launches"},
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(ach / pk["hbm_gbs"], 3), "traffic": None, "peak_kind": kind},
+                         "frac": round(ach / pk["hbm_gbs"], 3), "traffic": int(byts * ATTN_TRAFFIC_PER_ALG_BYTE),
+                         "traffic_source": ATTN_TRAFFIC_SOURCE, "peak_kind": kind},
             "gpu_launches": 2 * args.steps, "clocks": clk.summary()}
 
 

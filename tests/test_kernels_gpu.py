@@ -247,8 +247,7 @@ def test_splitk_gemm_add_rmsnorm(cuda, M, N, Kd):
     w = (torch.randn((N, Kd), generator=g) * 0.02).to(BF).to(cuda)
     res0 = torch.randn((M, N), generator=g).to(BF).to(cuda)
     nw = (1 + 0.1 * torch.randn(N, generator=g)).to(BF).to(cuda)
-    splits = K().pick_splits(M, N, Kd)
-    assert splits > 1
+    splits = max(2, K().pick_splits(M, N, Kd))  # exercise split-K even where the heuristic picks 1
     part = torch.empty((splits, M, N), dtype=torch.float32, device=cuda)
     K().gemm_splitk(x, w, part, splits)
     ref_f32 = x.float() @ w.float().t()
@@ -285,8 +284,7 @@ def test_splitk_qkv_and_silu_epilogues(cuda, M):
     caches = [torch.zeros((nb, hkv, bs, 128), dtype=BF, device=cuda) for _ in range(4)]
     q1 = K().qkv_norm_rope_store(x, wqkv, qn, kn, eps, pos, table, slots, caches[0], caches[1], hq)
     N = wqkv.shape[0]
-    splits = K().pick_splits(M, N, H)
-    assert splits > 1
+    splits = max(2, K().pick_splits(M, N, H))
     part = torch.empty((splits, M, N), dtype=torch.float32, device=cuda)
     K().gemm_splitk(x, wqkv, part, splits)
     q2 = torch.empty_like(q1)
