@@ -100,7 +100,8 @@ def clear_device_error() -> None:
 
 DEVICE_ERRORS = {1: "block id outside the KV pool", 2: "cache slot outside the KV pool",
                  4: "device wait timed out", 8: "position outside the RoPE table",
-                 16: "token id outside the vocabulary", 32: "context longer than the block table"}
+                 16: "token id outside the vocabulary", 32: "context longer than the block table",
+                 64: "a peer GPU did not arrive in the TP exchange"}
 
 
 def raise_on_device_error(what: str = "kernel") -> None:

@@ -33,7 +33,13 @@
 // every peer's words of call c + 1, which each peer writes only after its
 // call c kernel (and so its reads of the parity-c buffer) completed, so two
 // buffers suffice.  Every wait gives up after kPeerWaitNs, reports
-// ERR_PEER_TIMEOUT and lets the kernel finish (the output is then invalid).
+// ERR_PEER_TIMEOUT, poisons this rank's buffer and lets the kernel finish
+// (the output is then invalid).  A timed-out call leaves the ranks out of
+// step for good (later calls would each wait out the limit), so every later
+// call on a poisoned buffer skips its waits and the host, which reads the
+// error word after each step, raises.  The limit is long (20 s) because a
+// rank's host can stall for seconds (a large pickle, a garbage collection)
+// while its peers are already waiting on the GPU.
 #include <cstring>
 
 #include "common.cuh"
@@ -44,14 +50,15 @@ namespace aacc {
 
 constexpr int kArMaxWorld = 8;
 constexpr int kArSlots = 128;
-constexpr int64_t kArHeaderBytes = 16384;  // seen[kArSlots], padded
-constexpr uint64_t kPeerWaitNs = 2000000000ull;
+constexpr int64_t kArHeaderBytes = 16384;  // seen[kArSlots] | poison word at 8192, padded
+constexpr uint64_t kPeerWaitNs = 20000000000ull;
 
 struct ArPeers {
   char* buf[kArMaxWorld];
 };
 
 __device__ __forceinline__ uint32_t* ar_seen(char* b) { return reinterpret_cast<uint32_t*>(b); }
+__device__ __forceinline__ uint32_t* ar_poison(char* b) { return reinterpret_cast<uint32_t*>(b + 8192); }
 
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
@@ -68,7 +75,8 @@ __device__ __forceinline__ void st_flagged(uint64_t* dst, uint4 v, uint32_t seq)
 }
 
 // Wait until the four flagged words at src carry `seq` and return their data.
-__device__ __forceinline__ uint4 ld_flagged(const uint64_t* src, uint32_t seq, unsigned* err, bool& ok) {
+__device__ __forceinline__ uint4 ld_flagged(const uint64_t* src, uint32_t seq, unsigned* err, bool& ok,
+                                            uint32_t* poison) {
   uint64_t a, b, c, d;
   uint64_t t0 = 0;
   for (uint32_t i = 0;; ++i) {
@@ -84,6 +92,7 @@ __device__ __forceinline__ uint4 ld_flagged(const uint64_t* src, uint32_t seq, u
         t0 = now;
       } else if (now - t0 > kPeerWaitNs || i > (1u << 28)) {
         report(err, ERR_PEER_TIMEOUT);
+        atomicExch(poison, 1u);
         ok = false;
         break;
       }
@@ -132,7 +141,9 @@ __global__ void __launch_bounds__(kNormMaxThreads)
     return reinterpret_cast<uint64_t*>(b + kArHeaderBytes) + (2 * world * max_rows + par * max_rows + m) * row_words +
            c * 4;
   };
-  bool ok = true;
+  // A poisoned buffer (an earlier call timed out) skips every wait.
+  bool ok = *reinterpret_cast<volatile uint32_t*>(ar_poison(own)) == 0;
+  uint32_t* poison = ar_poison(own);
   // The first row's residual is local and already final: load it now so its
   // latency hides under the exchange.
   uint4 res0[V];
@@ -167,7 +178,7 @@ __global__ void __launch_bounds__(kNormMaxThreads)
     for (int64_t m = j; m < M; m += kArSlots) {
       for (int c = rank * slice + tid; c < (rank + 1) * slice; c += nt) {
         float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int from = 0; from < world; ++from) add8(a, ld_flagged(recv1(own, from, m, c), seq, err, ok));
+        for (int from = 0; from < world; ++from) add8(a, ld_flagged(recv1(own, from, m, c), seq, err, ok, poison));
         const uint4 pk = pack8(a);
         for (int p = 0; p < world; ++p) st_flagged(recv2(peers.buf[(rank + p) % world], m, c), pk, seq);
       }
@@ -182,7 +193,7 @@ __global__ void __launch_bounds__(kNormMaxThreads)
       const int c = v * nt + tid;
       float d[8];
       if (kTwoShot) {
-        const uint4 u = ld_flagged(recv2(own, m, c), seq, err, ok);
+        const uint4 u = ld_flagged(recv2(own, m, c), seq, err, ok, poison);
         float2 f;
         f = unpack_bf16(u.x); d[0] = f.x; d[1] = f.y;
         f = unpack_bf16(u.y); d[2] = f.x; d[3] = f.y;
@@ -191,7 +202,7 @@ __global__ void __launch_bounds__(kNormMaxThreads)
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) d[i] = 0.f;
-        for (int from = 0; from < world; ++from) add8(d, ld_flagged(recv1(own, from, m, c), seq, err, ok));
+        for (int from = 0; from < world; ++from) add8(d, ld_flagged(recv1(own, from, m, c), seq, err, ok, poison));
 #pragma unroll
         for (int i = 0; i < 8; ++i) d[i] = rbf(d[i]);
       }

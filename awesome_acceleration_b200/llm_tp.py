@@ -27,6 +27,7 @@ import time
 
 import torch
 
+from . import _lib
 from .llm import GenerationOutput, _Request, kv_sized_max_seqs, sampling_seed
 from .model import distributed as D
 from .model.model import Qwen3Config, Qwen3ForCausalLM
@@ -310,6 +311,8 @@ class LLMTP:
                 staged = slots
             rt.decode_step(slots)
             sampled = rt.read_tokens(B)
+            if self.tp_size > 1:  # a timed-out NVLink exchange leaves the group out of step: stop, do not crawl on
+                _lib.raise_on_device_error("TP decode step")
             released = []
             for slot, tok in zip(slots, sampled):
                 st = active[slot]

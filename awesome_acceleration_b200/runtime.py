@@ -272,18 +272,22 @@ class Qwen3Runtime:
         output is all-reduced first (RowParallelLinear, parallel_layers.py:190-195)."""
         M = inp.shape[0]
         splits = self._splits(M, w, part)
+        # The NVLink exchange only runs inside captured decode graphs: there the
+        # ranks replay in step, while eager launches (prefill, capture warm-up)
+        # can lag by a host stall, which NCCL's blocking collectives absorb.
+        graph = self.comm.size > 1 and torch.cuda.is_current_stream_capturing()
         if splits > 1:
             pv = part[:splits * M * w.shape[0]].view(splits, M, w.shape[0])
             K.gemm_splitk(inp, w, pv, splits)
             if self.comm.size == 1:
                 K.splitk_add_rmsnorm(pv, splits, res, norm_w, self.eps, out=x)
                 return
-            if self.comm.allreduce_add_rmsnorm(pv, splits, res, norm_w, self.eps, x):
+            if graph and self.comm.allreduce_add_rmsnorm(pv, splits, res, norm_w, self.eps, x):
                 return
             K.splitk_reduce(pv, splits, delta)
         else:
             K.gemm(inp, w, out=delta)
-            if self.comm.size > 1 and self.comm.allreduce_add_rmsnorm(delta, 0, res, norm_w, self.eps, x):
+            if graph and self.comm.size > 1 and self.comm.allreduce_add_rmsnorm(delta, 0, res, norm_w, self.eps, x):
                 return
         self.comm.all_reduce(delta)
         K.add_rmsnorm(delta, res, norm_w, self.eps, out=x)

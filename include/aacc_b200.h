@@ -300,8 +300,10 @@ int aacc_peer_buffer_free(void* ptr);
  * M (<= max_rows), world and two_shot, in stream order.  one-shot
  * (two_shot = 0) pushes the whole output to every rank; two-shot
  * reduce-scatters by columns and all-gathers the reduced slices.  A peer that
- * does not arrive within 2 s sets the device error word (bit 64) and the
- * output is invalid.  Replaces RowParallelLinear's dist.all_reduce
+ * does not arrive within 20 s sets the device error word (bit 64), poisons
+ * this rank's exchange buffer (every later call skips its waits) and the
+ * output is invalid; the caller reads the error word and gives up on the
+ * group.  Replaces RowParallelLinear's dist.all_reduce
  * (parallel_layers.py:190-195) plus the residual add and RMSNorm after it
  * (model/model.py:259-265; model/model_tp.py:311-322). */
 int aacc_tp_allreduce_add_rmsnorm(const void* src, int splits, void* const* buffers, int world, int rank,

@@ -149,6 +149,115 @@ def _exit_propagates(rank, world):
     assert time.time() - t0 < 60
 
 
+def _engine_protocol(rank, world, n_req, slots, seed):
+    """LLMTP's own leader / worker loops on CPU ranks, over a stand-in runtime
+    that logs every step it is told to run (and joins a Gloo collective at
+    each, as the real one joins NCCL): a continuous-batching job with more
+    requests than slots, ragged prompts, per-request max_tokens and
+    temperatures must take every rank through the same steps, in the same
+    order, and finish every request."""
+    import itertools
+    import queue
+    import random
+    import torch.distributed as dist
+    from awesome_acceleration_b200 import llm_tp
+    from awesome_acceleration_b200.model import distributed as D
+    from awesome_acceleration_b200.runtime import Qwen3Runtime
+    D.init_distributed(world, backend="gloo", timeout_s=30)
+    log = []
+
+    class KV:
+        def __init__(self):
+            self.lengths = {}
+
+        def reserve(self, r, n):
+            assert n <= 4096
+
+        def release(self, r):
+            self.lengths.pop(r, None)
+
+    class Buf:
+        meta = torch.zeros((4, slots), dtype=torch.int64)
+        temp = torch.zeros(slots, dtype=torch.float32)
+
+    class RT:
+        max_batch, use_graphs, buf = slots, True, Buf()
+        padded_batch = Qwen3Runtime.padded_batch
+
+        def load_decode_inputs(self, ids, positions, rows, temperatures=None, seeds=None):
+            B, Bp = len(rows), self.padded_batch(len(rows))
+            m = self.buf.meta
+            m[:, :Bp] = 0
+            m[2, :Bp] = -1
+            m[0, :B], m[1, :B], m[2, :B] = torch.tensor(ids), torch.tensor(positions), torch.tensor(rows)
+            m[3, :B] = torch.tensor(seeds or [0] * B)
+            self.buf.temp[:Bp] = 0
+            self.buf.temp[:B] = torch.tensor(temperatures or [0.0] * B)
+
+        def prefill(self, seqs, rows, temperatures=None, seeds=None):
+            log.append(("prefill", tuple(rows), tuple(len(q) for q in seqs), tuple(temperatures or ()),
+                        tuple(seeds or ())))
+            dist.all_reduce(torch.ones(1), group=D.get_tp_group())
+            for r, q in zip(rows, seqs):
+                kv.lengths[r] = len(q)
+            return torch.tensor([(sum(q) + len(q)) % 997 for q in seqs])
+
+        def decode_step(self, rows):
+            B, Bp = len(rows), self.padded_batch(len(rows))
+            m = self.buf.meta
+            log.append(("decode", Bp, tuple(m[2, :Bp].tolist()), tuple(m[1, :B].tolist()), tuple(m[3, :B].tolist()),
+                        tuple(self.buf.temp[:B].tolist())))
+            dist.all_reduce(torch.ones(1), group=D.get_tp_group())
+            m[0, :B] = (m[0, :B] * 31 + m[1, :B]) % 997
+            m[1, :B] += 1
+            for r in rows:
+                kv.lengths[r] += 1
+
+        def read_tokens(self, B):
+            return self.buf.meta[0, :B].tolist()
+
+    kv, rt = KV(), RT()
+
+    class Model:
+        max_batch = slots
+
+        def __init__(self):
+            self.kv = kv
+
+        def _rt(self):
+            return rt
+
+        def clear_all_slots(self):
+            kv.lengths.clear()
+
+    torch.cuda.synchronize = lambda *a, **k: None  # this process has no GPU work to wait for
+    llm_tp._lib.raise_on_device_error = lambda *a, **k: None  # nor a device error word
+    eng = llm_tp.LLMTP.__new__(llm_tp.LLMTP)
+    eng.device = torch.device("cpu")
+    eng.model, eng.max_num_seqs, eng.max_seq_len = Model(), slots, 4096
+    eng.config = type("C", (), {"eos_token_id": -1})()
+    eng.tp_size, eng.tp_rank, eng.is_tp_leader = world, rank, rank == 0
+    eng._bcast = torch.zeros(5 * slots, dtype=torch.int64)
+    eng._request_queue = queue.Queue() if rank == 0 else None
+    eng._loop_running, eng._loop_thread, eng._loop_error, eng.tokenizer = False, None, None, None
+    eng._base_seed, eng._serials = 3, itertools.count(1)
+    if rank == 0:
+        rnd = random.Random(seed)
+        reqs = [([rnd.randrange(1000) for _ in range(rnd.randint(1, 60))], rnd.choice([1, 2, 5, 9, 17, 30]),
+                 rnd.choice([0.0, 0.0, 0.7])) for _ in range(n_req)]
+        futs = [eng.generate_ids([p], max_tokens=m, temperature=t, ignore_eos=True) for p, m, t in reqs]
+        outs = [f.result(timeout=60)[0] for f in futs]
+        eng.stop()
+        assert [o.generated_tokens for o in outs] == [m for _, m, _ in reqs]
+        assert eng._loop_error is None, eng._loop_error
+    else:
+        eng.serve_worker()
+    logs = [None] * world
+    dist.all_gather_object(logs, log, group=D.get_tp_cpu_group())
+    assert all(lg == logs[0] for lg in logs), "ranks ran different step sequences"
+    assert any(e[0] == "decode" and e[1] != len([r for r in e[2] if r >= 0]) for e in logs[0])  # padded buckets ran
+
+
 # ---------------------------------------------------------------------------- tests
 @pytest.mark.parametrize("world,tp", [(2, 2), (4, 2), (4, 4)])
 def test_process_groups(world, tp):
@@ -179,3 +288,9 @@ def test_dead_worker_raises_instead_of_hanging():
         p.join(timeout=30)
         if p.is_alive():
             p.kill()
+
+
+@pytest.mark.parametrize("world,n_req,slots", [(2, 40, 12), (3, 90, 40)])
+def test_llmtp_leader_worker_protocol(world, n_req, slots):
+    res = spawn(world, _engine_protocol, n_req, slots, world * 1000 + n_req)
+    assert all(v is None for v in res.values()), res
