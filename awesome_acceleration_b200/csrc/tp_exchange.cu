@@ -32,7 +32,7 @@
 // the parity of c: a rank starts writing call c + 2 only after it received
 // every peer's words of call c + 1, which each peer writes only after its
 // call c kernel (and so its reads of the parity-c buffer) completed, so two
-// buffers suffice.  Every wait gives up after kPeerWaitNs, reports
+// buffers suffice.  Every wait gives up after the peer wait limit, reports
 // ERR_PEER_TIMEOUT, poisons this rank's buffer and lets the kernel finish
 // (the output is then invalid).  A timed-out call leaves the ranks out of
 // step for good (later calls would each wait out the limit), so every later
@@ -51,7 +51,8 @@ namespace aacc {
 constexpr int kArMaxWorld = 8;
 constexpr int kArSlots = 128;
 constexpr int64_t kArHeaderBytes = 16384;  // seen[kArSlots] | poison word at 8192, padded
-constexpr uint64_t kPeerWaitNs = 20000000000ull;
+constexpr int64_t kDefaultPeerWaitMs = 20000;
+static int64_t g_peer_wait_ms = kDefaultPeerWaitMs;  // host-side setting, passed to every launch
 
 struct ArPeers {
   char* buf[kArMaxWorld];
@@ -76,7 +77,7 @@ __device__ __forceinline__ void st_flagged(uint64_t* dst, uint4 v, uint32_t seq)
 
 // Wait until the four flagged words at src carry `seq` and return their data.
 __device__ __forceinline__ uint4 ld_flagged(const uint64_t* src, uint32_t seq, unsigned* err, bool& ok,
-                                            uint32_t* poison) {
+                                            uint32_t* poison, uint64_t wait_ns) {
   uint64_t a, b, c, d;
   uint64_t t0 = 0;
   for (uint32_t i = 0;; ++i) {
@@ -87,10 +88,14 @@ __device__ __forceinline__ uint4 ld_flagged(const uint64_t* src, uint32_t seq, u
       break;
     if (!ok) break;  // an earlier wait of this thread already timed out
     if ((i & 15) == 0) {
+      if (*reinterpret_cast<volatile uint32_t*>(poison)) {  // another thread of this rank gave up already
+        ok = false;
+        break;
+      }
       const uint64_t now = global_ns();
       if (i == 0) {
         t0 = now;
-      } else if (now - t0 > kPeerWaitNs || i > (1u << 28)) {
+      } else if (now - t0 > wait_ns || i > (1u << 28)) {
         report(err, ERR_PEER_TIMEOUT);
         atomicExch(poison, 1u);
         ok = false;
@@ -122,7 +127,7 @@ __global__ void __launch_bounds__(kNormMaxThreads)
     tp_allreduce_norm_kernel(const void* __restrict__ src, int splits, const __grid_constant__ ArPeers peers,
                              int world, int rank, int64_t max_rows, bf16* __restrict__ residual,
                              const bf16* __restrict__ w, bf16* __restrict__ y, int64_t M, int hidden, float eps,
-                             unsigned* err) {
+                             unsigned* err, uint64_t wait_ns) {
   griddep_wait();
   griddep_launch();
   const int j = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
@@ -178,7 +183,7 @@ __global__ void __launch_bounds__(kNormMaxThreads)
     for (int64_t m = j; m < M; m += kArSlots) {
       for (int c = rank * slice + tid; c < (rank + 1) * slice; c += nt) {
         float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int from = 0; from < world; ++from) add8(a, ld_flagged(recv1(own, from, m, c), seq, err, ok, poison));
+        for (int from = 0; from < world; ++from) add8(a, ld_flagged(recv1(own, from, m, c), seq, err, ok, poison, wait_ns));
         const uint4 pk = pack8(a);
         for (int p = 0; p < world; ++p) st_flagged(recv2(peers.buf[(rank + p) % world], m, c), pk, seq);
       }
@@ -193,7 +198,7 @@ __global__ void __launch_bounds__(kNormMaxThreads)
       const int c = v * nt + tid;
       float d[8];
       if (kTwoShot) {
-        const uint4 u = ld_flagged(recv2(own, m, c), seq, err, ok, poison);
+        const uint4 u = ld_flagged(recv2(own, m, c), seq, err, ok, poison, wait_ns);
         float2 f;
         f = unpack_bf16(u.x); d[0] = f.x; d[1] = f.y;
         f = unpack_bf16(u.y); d[2] = f.x; d[3] = f.y;
@@ -202,7 +207,7 @@ __global__ void __launch_bounds__(kNormMaxThreads)
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) d[i] = 0.f;
-        for (int from = 0; from < world; ++from) add8(d, ld_flagged(recv1(own, from, m, c), seq, err, ok, poison));
+        for (int from = 0; from < world; ++from) add8(d, ld_flagged(recv1(own, from, m, c), seq, err, ok, poison, wait_ns));
 #pragma unroll
         for (int i = 0; i < 8; ++i) d[i] = rbf(d[i]);
       }
@@ -232,6 +237,13 @@ __global__ void __launch_bounds__(kNormMaxThreads)
 using namespace aacc;
 
 extern "C" {
+
+int aacc_tp_set_peer_wait_ms(int64_t ms) {
+  if (ms < 1 || ms > 600000) return set_error(AACC_ERR_INVALID, "tp_set_peer_wait_ms: %lld ms outside [1, 600000]",
+                                              (long long)ms);
+  g_peer_wait_ms = ms;
+  return AACC_OK;
+}
 
 int64_t aacc_tp_exchange_bytes(int world, int64_t max_rows, int64_t hidden) {
   if (world < 1 || max_rows < 1 || hidden < 1) return 0;
@@ -302,14 +314,15 @@ int aacc_tp_allreduce_add_rmsnorm(const void* src, int splits, void* const* buff
     peers.buf[p] = static_cast<char*>(buffers[p]);
   }
   unsigned* err = device_error_ptr();
+  const uint64_t wait_ns = (uint64_t)g_peer_wait_ms * 1000000ull;
   cudaError_t le;
 #define AACC_AR_LAUNCH(VV)                                                                                        \
   le = two_shot ? launch_k(tp_allreduce_norm_kernel<VV, true>, dim3(kArSlots), dim3(threads), 0, stream, src,    \
                            splits, peers, world, rank, max_rows, (bf16*)residual, (const bf16*)w, (bf16*)y, M,  \
-                           (int)hidden, eps, err)                                                                \
+                           (int)hidden, eps, err, wait_ns)                                                                \
                 : launch_k(tp_allreduce_norm_kernel<VV, false>, dim3(kArSlots), dim3(threads), 0, stream, src,   \
                            splits, peers, world, rank, max_rows, (bf16*)residual, (const bf16*)w, (bf16*)y, M,  \
-                           (int)hidden, eps, err)
+                           (int)hidden, eps, err, wait_ns)
   switch (V) {
     case 1: AACC_AR_LAUNCH(1); break;
     case 2: AACC_AR_LAUNCH(2); break;

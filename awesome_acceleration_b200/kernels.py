@@ -268,6 +268,11 @@ def argmax_merge(cand_val, cand_idx, tokens=None):
     return tokens
 
 
+def tp_set_peer_wait_ms(ms: int) -> None:
+    """How long an exchange waits for a peer before it reports ERR_PEER_TIMEOUT (default 20 s)."""
+    _lib.check(_lib_().aacc_tp_set_peer_wait_ms(int(ms)), "tp_set_peer_wait_ms")
+
+
 def tp_exchange_bytes(world: int, max_rows: int, hidden: int) -> int:
     return int(_lib_().aacc_tp_exchange_bytes(world, max_rows, hidden))
 

@@ -289,6 +289,12 @@ int aacc_peer_buffer_open(const void* ipc_handle, void** ptr);
 int aacc_peer_buffer_close(void* peer_ptr);
 int aacc_peer_buffer_free(void* ptr);
 
+/* Limit, in ms (default 20000), after which a wait for a peer in
+ * aacc_tp_allreduce_add_rmsnorm gives up (applies to later launches and
+ * graph captures).  No counterpart in the reference (NCCL waits for its
+ * watchdog). */
+int aacc_tp_set_peer_wait_ms(int64_t ms);
+
 /* RowParallel all-reduce fused with the residual add and the next RMSNorm,
  * over the group's exchange buffers (buffers[p] = rank p's buffer as mapped in
  * this process, buffers[rank] = this rank's own):

@@ -453,3 +453,40 @@ def test_temperature_sampling_distribution(cuda):
     emp = np.bincount(tok.cpu().numpy(), minlength=V) / M
     tv = 0.5 * np.abs(emp - p).sum()
     assert tv < 0.08, tv  # TV of 4096 draws from the right distribution stays well below this
+
+
+def test_tp_exchange_wait_runs_out_and_poisons(cuda):
+    """A peer that never arrives, on one GPU and without a fault: the 'peer'
+    of a two-rank exchange is a second local buffer nothing writes into.  The
+    bounded wait runs out, sets the device error word and poisons this rank's
+    buffer; the next call then skips its waits and returns at once."""
+    import time
+    H, M, max_rows = 1024, 4, 8
+    nbytes = K().tp_exchange_bytes(2, max_rows, H)
+    own = torch.zeros(nbytes, dtype=torch.uint8, device=cuda)
+    ghost = torch.zeros(nbytes, dtype=torch.uint8, device=cuda)
+    src = torch.randn(M, H, device=cuda).to(BF)
+    res = torch.randn(M, H, device=cuda).to(BF)
+    w = torch.ones(H, dtype=BF, device=cuda)
+    y = torch.empty_like(res)
+    bufs = [own.data_ptr(), ghost.data_ptr()]
+    clear_err()
+    K().tp_set_peer_wait_ms(200)
+    try:
+        torch.cuda.synchronize()
+        t0 = time.time()
+        K().tp_allreduce_add_rmsnorm(src, 0, bufs, 0, max_rows, res, w, 1e-6, y, two_shot=True)
+        torch.cuda.synchronize()
+        t1 = time.time()
+        assert dev_err() & 64
+        assert own[8192:8196].view(torch.int32).item() == 1  # poisoned
+        clear_err()
+        K().tp_allreduce_add_rmsnorm(src, 0, bufs, 0, max_rows, res, w, 1e-6, y, two_shot=True)
+        torch.cuda.synchronize()
+        t2 = time.time()
+        assert 0.15 <= t1 - t0 < 10, t1 - t0
+        assert t2 - t1 < 0.15, t2 - t1  # a poisoned buffer does not wait
+        assert dev_err() == 0
+    finally:
+        K().tp_set_peer_wait_ms(20000)
+        clear_err()
