@@ -1,0 +1,52 @@
+"""Host-side policies of the B200 runtime that need no GPU: split-K choice,
+decode-batch buckets, sampling seeds, the gate/up interleave."""
+import torch
+
+from awesome_acceleration_b200.kernels import pick_splits
+from awesome_acceleration_b200.llm import sampling_seed
+from awesome_acceleration_b200.runtime import Qwen3Runtime, interleave_gate_up
+
+
+def test_pick_splits_invariants_and_cfg2_choices():
+    for M in (1, 16, 128, 200, 256, 512):
+        for N, K in ((4096, 1024), (6144, 1024), (1024, 2048), (1024, 3072), (1536, 4096), (4096, 1536)):
+            d = pick_splits(M, N, K, max_elems=8 << 20)
+            tiles = ((N + 127) // 128) * ((M + 127) // 128)
+            assert (K // 64) % d == 0 and (d == 1 or tiles * d <= 148) and d * M * N <= 8 << 20
+            assert d == 1 or 2 * d * M <= K  # fp32 partials no more bytes than the weights
+    # the cfg2 decode step (M = 256): QKV 2, gate/up 1, o_proj 4, down_proj 6
+    assert [pick_splits(256, n, k, max_elems=8 << 20) for n, k in ((4096, 1024), (6144, 1024), (1024, 2048),
+                                                                    (1024, 3072))] == [2, 1, 4, 6]
+
+
+class _Rt:
+    padded_batch = Qwen3Runtime.padded_batch
+
+    def __init__(self, max_batch, graphs=True):
+        self.max_batch, self.use_graphs = max_batch, graphs
+
+
+def test_decode_batch_buckets():
+    rt = _Rt(512)
+    sizes = [rt.padded_batch(b) for b in range(1, 513)]
+    assert all(b <= p <= 512 for b, p in zip(range(1, 513), sizes))
+    assert sizes == sorted(sizes) and len(set(sizes)) <= 25  # 4 powers of two, 7 multiples of 8, 14 of 32
+    assert [rt.padded_batch(b) for b in (1, 3, 5, 9, 63, 65, 256, 257)] == [1, 4, 8, 16, 64, 96, 256, 288]
+    assert _Rt(434).padded_batch(430) == 434  # capped at max_batch
+    assert _Rt(512, graphs=False).padded_batch(37) == 37  # eager runs the exact size
+
+
+def test_sampling_seeds_are_distinct_int64():
+    seeds = {sampling_seed(b, s, i) for b in (0, 1, 7) for s in range(1, 200) for i in range(8)}
+    assert len(seeds) == 3 * 199 * 8
+    assert all(0 <= x < 2 ** 63 for x in seeds)
+
+
+def test_gate_up_interleave_groups_of_64():
+    I, H = 256, 8
+    gate = torch.arange(I).float().unsqueeze(1).expand(I, H)
+    up = (1000 + torch.arange(I)).float().unsqueeze(1).expand(I, H)
+    w = interleave_gate_up(gate, up)
+    for j in range(I // 64):
+        assert torch.equal(w[128 * j:128 * j + 64, 0], torch.arange(64 * j, 64 * j + 64).float())
+        assert torch.equal(w[128 * j + 64:128 * j + 128, 0], 1000 + torch.arange(64 * j, 64 * j + 64).float())
