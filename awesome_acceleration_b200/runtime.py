@@ -395,10 +395,14 @@ class Qwen3Runtime:
         self.h2d_bytes += 2 * Bp * 8
 
     def reserve_decode(self, rows) -> None:
-        """Host block bookkeeping for one decode step of `rows` (new token at lengths[row])."""
+        """Host block bookkeeping for one decode step of `rows` (new token at
+        lengths[row]).  Vectorised: only rows whose new token opens a block
+        go through reserve (once every block_size steps)."""
         kv = self.kv
-        for r in rows:
-            kv.reserve(r, int(kv.lengths[r]) + 1)
+        r = np.asarray(rows, dtype=np.int64)
+        need = (kv.lengths[r] + kv.block_size) // kv.block_size  # blocks for lengths + 1 tokens
+        for i in np.nonzero(need > kv._nblk[r])[0]:
+            kv.reserve(int(r[i]), int(kv.lengths[r[i]]) + 1)
         kv.sync()
 
     def decode_step(self, rows, logits: torch.Tensor | None = None) -> torch.Tensor:
@@ -416,8 +420,7 @@ class Qwen3Runtime:
             g.replay()
             self.graph_replays += 1
             self.replayed_launches += self.graph_launches[Bp]
-        for r in rows:
-            self.kv.lengths[r] += 1
+        self.kv.lengths[np.asarray(rows, dtype=np.int64)] += 1
         return self.buf.ids[:B]
 
     def capture_buckets(self, max_rows: int | None = None) -> None:
