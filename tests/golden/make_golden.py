@@ -133,9 +133,12 @@ def run_case(ref_llm, ref_model, name, spec):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("AACC_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("AACC_REFERENCE"),
+                    help="checkout of the reference project (or set AACC_REFERENCE)")
     ap.add_argument("--cases", nargs="*", default=list(CASES))
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("pass --reference <path to the reference checkout> or set AACC_REFERENCE")
     torch.set_num_threads(os.cpu_count() or 8)
     ref_llm, ref_model = load_reference(args.reference)
     for name in args.cases:
