@@ -691,7 +691,7 @@ def main():
     try:
         line = {"attn": run_attn, "gemm": run_gemm, "cfg2": run_cfg2, "cfg4": run_cfg4,
                 "cfg5": run_cfg5}[args.workload](args, device)
-        if args.rank == 0 and args.workload == "cfg2" and not (args.no_cpu_baseline or args.profile):
+        if args.world == 1 and args.workload == "cfg2" and not (args.no_cpu_baseline or args.profile):
             v, info = cpu_sample()
             line["cpu_baseline"] = {"value": round(v, 3), "unit": "output tok/s", "cores": info["cores"],
                                     "kind": "port", "sample": info["sample"]}
