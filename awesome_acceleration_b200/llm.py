@@ -70,6 +70,8 @@ def kv_sized_max_seqs(config: Qwen3Config, max_num_seqs: int, max_seq_len: int, 
     reserve.  Called once the weights are on the device, it also keeps the
     memory they already hold and one prefill chunk's activations out of the
     KV budget: the reference's fixed reserve only covers a 0.6B model."""
+    torch.cuda.synchronize(device)
+    torch.cuda.empty_cache()  # blocks the allocator caches (e.g. weight-init temporaries) are free for the KV pool
     free, total = torch.cuda.mem_get_info(device)
     per_tok = 2 * config.num_key_value_heads * config.head_dim * 2 * config.num_hidden_layers // tp_size
     q_cols = config.num_attention_heads * config.head_dim // tp_size
@@ -105,12 +107,12 @@ class LLM:
         if model_path is not None and os.path.exists(os.path.join(model_path, "tokenizer_config.json")):
             from transformers import AutoTokenizer
             self.tokenizer = AutoTokenizer.from_pretrained(model_path, trust_remote_code=True)
-        self.max_num_seqs = kv_sized_max_seqs(self.config, max_num_seqs, max_seq_len, 3.0, self.device,
-                                              prefill_chunk_tokens=prefill_chunk_tokens)
         self.model.eval()
         self.model.use_cuda_graphs = use_cuda_graphs
         self.model.prefill_chunk_tokens = prefill_chunk_tokens
-        self.model.fuse_qkv()
+        self.model.fuse_qkv()  # before sizing: the fused weights are what stays resident
+        self.max_num_seqs = kv_sized_max_seqs(self.config, max_num_seqs, max_seq_len, 3.0, self.device,
+                                              prefill_chunk_tokens=prefill_chunk_tokens)
         self.model.init_kv_cache(self.max_num_seqs, max_seq_len, self.device, dtype, block_size=block_size)
         self._request_queue: queue.Queue[_Request] = queue.Queue()
         self._base_seed = int(seed)  # sampling noise: one stream per (request, prompt)

@@ -80,16 +80,16 @@ class LLMTP:
                 os.path.exists(os.path.join(model_path, "tokenizer_config.json")):
             from transformers import AutoTokenizer
             self.tokenizer = AutoTokenizer.from_pretrained(model_path, trust_remote_code=True)
+        self.model.eval()
+        self.model.use_cuda_graphs = use_cuda_graphs
+        self.model.prefill_chunk_tokens = prefill_chunk_tokens
+        self.model.fuse_qkv()  # before sizing: the fused weights are what stays resident
         self.max_num_seqs = kv_sized_max_seqs(self.config, max_num_seqs, max_seq_len, 15.0, self.device, self.tp_size,
                                               prefill_chunk_tokens)
         if self.tp_size > 1:  # free memory differs a little per GPU; the group must agree on slots and buckets
             n = torch.tensor([self.max_num_seqs], dtype=torch.int64)
             torch.distributed.all_reduce(n, op=torch.distributed.ReduceOp.MIN, group=D.get_tp_cpu_group())
             self.max_num_seqs = int(n.item())
-        self.model.eval()
-        self.model.use_cuda_graphs = use_cuda_graphs
-        self.model.prefill_chunk_tokens = prefill_chunk_tokens
-        self.model.fuse_qkv()
         self.model.init_kv_cache(self.max_num_seqs, max_seq_len, self.device, dtype, block_size=block_size)
         self._bcast = torch.zeros(5 * self.model.max_batch, dtype=torch.int64, device=self.device)
         self._base_seed = int(seed)  # sampling noise: one stream per (request, prompt)

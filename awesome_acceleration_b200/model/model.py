@@ -131,8 +131,15 @@ class MLP(nn.Module):
         self._gate_up = None
 
     def fuse_gate_up(self):
+        """Interleave gate/up rows into the layout the fused SiLU GEMM reads, then
+        release the separate gate/up weights (their values live on in the fused
+        copy), so the weights are held once."""
+        if self._gate_up is not None:
+            return
         with torch.no_grad():
             self._gate_up = interleave_gate_up(self.gate_proj.weight, self.up_proj.weight).contiguous()
+            for lin in (self.gate_proj, self.up_proj):
+                lin.weight.data = lin.weight.data.new_empty(0)
 
 
 class TransformerBlock(nn.Module):

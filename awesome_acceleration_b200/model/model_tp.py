@@ -70,8 +70,15 @@ class MLPTP(nn.Module):
         self._gate_up = None
 
     def fuse_gate_up(self):
+        """Interleave gate/up rows into the layout the fused SiLU GEMM reads, then
+        release the separate gate/up weights (their values live on in the fused
+        copy), so the weights are held once."""
+        if self._gate_up is not None:
+            return
         with torch.no_grad():
             self._gate_up = interleave_gate_up(self.gate_proj.weight, self.up_proj.weight).contiguous()
+            for lin in (self.gate_proj, self.up_proj):
+                lin.weight.data = lin.weight.data.new_empty(0)
 
 
 class TransformerBlockTP(nn.Module):
@@ -120,8 +127,12 @@ class Qwen3ForCausalLMTP(nn.Module):
         cut this rank's vocab shard of the lm_head."""
         for layer in self.model.layers:
             layer.mlp.fuse_gate_up()
+        if self._lm_shard is not None:
+            return
         w = self.model.embed_tokens.weight if self.lm_head is None else self.lm_head.weight
         self._lm_shard = split_tensor_along_dim(w.data, self.tp_size, dim=0)
+        if self.lm_head is not None and self.tp_size > 1 and self._lm_shard.data_ptr() != w.data_ptr():
+            self.lm_head.weight.data = w.data.new_empty(0)  # untied: only this rank's shard is used from here on
         self.runtime = None
 
     def init_kv_cache(self, num_slots: int, max_seq_len: int, device, dtype, *, block_size: int = 256,
