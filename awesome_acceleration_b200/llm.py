@@ -21,7 +21,6 @@ import os
 import queue
 import threading
 import time
-from collections import deque
 from dataclasses import dataclass, field
 
 import torch
@@ -261,67 +260,82 @@ class LLM:
         eos = self.config.eos_token_id
         self.model.clear_all_slots()
         staged: list[int] | None = None  # rows whose inputs the device buffers hold
-        decode_times = deque(maxlen=16)
-        while self._loop_running or pending or active:
+        # Decode steps launched but not read yet: (rows, read-back handle, launch time).  While
+        # the host reads step t's tokens and runs the stop checks, step t+1 already runs on the
+        # device (the graph takes its ids and positions from step t on the device).
+        inflight: list = []
+        t_last = time.perf_counter()
+        while self._loop_running or pending or active or inflight:
             # Phase 1: drain the queue.
             while True:
                 try:
                     pending.append(self._request_queue.get_nowait())
                 except queue.Empty:
                     break
-            if not pending and not active:
+            if not pending and not active and not inflight:
                 if not self._loop_running:
                     break
                 time.sleep(0.001)
                 continue
-            # Phase 2: lowest free slots to pending prompts.
-            new_work = []
-            for req in list(pending):
-                while req.pending_indices and free_slots:
-                    new_work.append((req, req.pending_indices.pop(0), free_slots.pop(0)))
-                if not req.pending_indices:
-                    pending.remove(req)
-            # Phase 3: prefill.
-            if new_work:
-                t0 = time.perf_counter()
-                seqs = [r.token_ids[i] for r, i, _ in new_work]
-                slots = [s for _, _, s in new_work]
-                # per-request temperature (the reference applies the first request's to the whole batch)
-                toks = rt.prefill(seqs, slots, temperatures=[r.temperature for r, _, _ in new_work],
-                                  seeds=[r.seeds[i] for r, i, _ in new_work]).tolist()
-                rt.d2h_bytes += 8 * len(toks)
-                self.stats["prefill_s"] += time.perf_counter() - t0
-                self.stats["prefill_tokens"] += sum(len(s) for s in seqs)
-                for (req, idx, slot), tok in zip(new_work, toks):
-                    plen = len(req.token_ids[idx])
-                    if 1 >= req.max_tokens or (not req.ignore_eos and tok == eos):
-                        self._finish(req, idx, [tok])
-                        kv.release(slot)
-                        bisect.insort(free_slots, slot)
-                    else:
-                        active[slot] = [req, idx, [tok], plen]
-                staged = None
-            if not active:
-                continue
-            # Phase 4: one decode step for every active sequence.
+            if not inflight:  # the batch only changes between steps that are all read
+                # Phase 2: lowest free slots to pending prompts.
+                new_work = []
+                for req in list(pending):
+                    while req.pending_indices and free_slots:
+                        new_work.append((req, req.pending_indices.pop(0), free_slots.pop(0)))
+                    if not req.pending_indices:
+                        pending.remove(req)
+                # Phase 3: prefill.
+                if new_work:
+                    t0 = time.perf_counter()
+                    seqs = [r.token_ids[i] for r, i, _ in new_work]
+                    slots = [s for _, _, s in new_work]
+                    # per-request temperature (the reference applies the first request's to the whole batch)
+                    toks = rt.prefill(seqs, slots, temperatures=[r.temperature for r, _, _ in new_work],
+                                      seeds=[r.seeds[i] for r, i, _ in new_work]).tolist()
+                    rt.d2h_bytes += 8 * len(toks)
+                    self.stats["prefill_s"] += time.perf_counter() - t0
+                    self.stats["prefill_tokens"] += sum(len(s) for s in seqs)
+                    for (req, idx, slot), tok in zip(new_work, toks):
+                        plen = len(req.token_ids[idx])
+                        if 1 >= req.max_tokens or (not req.ignore_eos and tok == eos):
+                            self._finish(req, idx, [tok])
+                            kv.release(slot)
+                            bisect.insort(free_slots, slot)
+                        else:
+                            active[slot] = [req, idx, [tok], plen]
+                    staged = None
+                if not active:
+                    continue
+            # Phase 4: decode steps.
             slots = list(active.keys())
-            B = len(slots)
-            if staged != slots:
-                rt.load_decode_inputs([active[s][2][-1] for s in slots], [active[s][3] for s in slots], slots,
-                                      temperatures=[active[s][0].temperature for s in slots],
-                                      seeds=[active[s][0].seeds[active[s][1]] for s in slots])
-                staged = slots
-            t0 = time.perf_counter()
-            rt.decode_step(slots)
-            sampled = rt.read_tokens(B)
-            dt = time.perf_counter() - t0
-            decode_times.append((B, dt))
-            self.stats["decode_s"] += dt
+            if not inflight:
+                if staged != slots:
+                    rt.load_decode_inputs([active[s][2][-1] for s in slots], [active[s][3] for s in slots], slots,
+                                          temperatures=[active[s][0].temperature for s in slots],
+                                          seeds=[active[s][0].seeds[active[s][1]] for s in slots])
+                    staged = slots
+                inflight.append(self._launch_step(rt, slots))
+            # Run one step ahead when that cannot change the batch: no row reaches its
+            # max_tokens / max_seq_len limit in the step being read (an EOS stop can still
+            # end a row; its extra token is dropped), and no waiting request could take a
+            # slot freed by it.
+            if (len(inflight) == 1 and inflight[0][0] == slots and not (pending and free_slots)
+                    and all(len(st[2]) + 1 < st[0].max_tokens and st[3] + 1 < self.max_seq_len
+                            for st in active.values())):
+                inflight.append(self._launch_step(rt, slots))
+            step_slots, handle, t0 = inflight.pop(0)
+            sampled = rt.wait_tokens(handle, len(step_slots))
+            now = time.perf_counter()
+            self.stats["decode_s"] += now - max(t0, t_last)
             self.stats["decode_steps"] += 1
-            # Phase 5: stop checks.
+            t_last = now
+            # Phase 5: stop checks (rows that ended at an earlier step are skipped).
             finished = False
-            for slot, tok in zip(slots, sampled):
-                st = active[slot]
+            for slot, tok in zip(step_slots, sampled):
+                st = active.get(slot)
+                if st is None:
+                    continue
                 st[2].append(tok)
                 st[3] += 1
                 req = st[0]
@@ -334,3 +348,10 @@ class LLM:
                     finished = True
             if finished:
                 staged = None
+
+    @staticmethod
+    def _launch_step(rt, slots):
+        """One decode step of `slots` plus the queued read-back of its tokens."""
+        t0 = time.perf_counter()
+        rt.decode_step(slots)
+        return slots, rt.copy_tokens_async(len(slots)), t0

@@ -228,6 +228,10 @@ class Qwen3Runtime:
         self._pinned = torch.zeros((4, max_batch), dtype=torch.int64).pin_memory()
         self._pinned_temp = torch.zeros(max_batch, dtype=torch.float32).pin_memory()
         self._tok_host = torch.zeros(max_batch, dtype=torch.int64).pin_memory()
+        # two pinned read-back buffers, so a step's tokens can be read while the next step runs
+        self._tok_ring = [torch.zeros(max_batch, dtype=torch.int64).pin_memory() for _ in range(2)]
+        self._tok_events = [torch.cuda.Event(), torch.cuda.Event()]
+        self._tok_next = 0
         # TP: RowParallel outputs of decode-sized batches go over NVLink peer memory
         # (one fused kernel) instead of NCCL + separate residual/norm kernels.
         self.comm.enable_peer_exchange(max_batch, hidden)
@@ -476,6 +480,23 @@ class Qwen3Runtime:
         torch.cuda.current_stream().synchronize()
         self.d2h_bytes += B * 8
         return t.tolist()
+
+    def copy_tokens_async(self, B: int) -> int:
+        """Queue the D2H of the last decode step's tokens into one of two pinned
+        buffers, behind that step on the stream (a later step overwriting the
+        device ids runs after the copy).  Returns the handle for wait_tokens;
+        each buffer is reused every second call."""
+        i = self._tok_next
+        self._tok_next ^= 1
+        self._tok_ring[i][:B].copy_(self.buf.ids[:B], non_blocking=True)
+        self._tok_events[i].record()
+        self.d2h_bytes += B * 8
+        return i
+
+    def wait_tokens(self, handle: int, B: int) -> list[int]:
+        """Tokens of a copy_tokens_async call (waits for that copy only)."""
+        self._tok_events[handle].synchronize()
+        return self._tok_ring[handle][:B].tolist()
 
     # ------------------------------------------------------------------ prefill
     def prefill(self, sequences: list[list[int]], rows: list[int], *, positions: list[list[int]] | None = None,
