@@ -23,6 +23,7 @@ SIGNATURES: dict[str, tuple] = {
     "aacc_last_error": (ctypes.c_char_p, []),
     "aacc_launch_count": (ctypes.c_ulonglong, []),
     "aacc_get_device_error": (I32, [P]),
+    "aacc_get_device_error_async": (I32, [P, P]),
     "aacc_clear_device_error": (I32, []),
     "aacc_kv_store": (I32, [P, P, I64, I64, I64, P, P, P, I64, I32, I32, P]),
     "aacc_decode_slot_mapping": (I32, [P, P, P, I64, I32, I64, P, I64, P]),

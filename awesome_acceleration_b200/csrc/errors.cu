@@ -108,6 +108,14 @@ int aacc_get_device_error(unsigned* out) {
   return AACC_OK;
 }
 
+int aacc_get_device_error_async(unsigned* out, cudaStream_t stream) {
+  if (!out) return aacc::set_error(AACC_ERR_INVALID, "null output");
+  cudaError_t e = cudaMemcpyFromSymbolAsync(out, aacc::g_device_error, sizeof(unsigned), 0, cudaMemcpyDeviceToHost,
+                                            stream);
+  if (e != cudaSuccess) return aacc::set_error(AACC_ERR_CUDA, "read device error: %s", cudaGetErrorString(e));
+  return AACC_OK;
+}
+
 int aacc_clear_device_error(void) {
   unsigned z = 0;
   cudaError_t e = cudaMemcpyToSymbol(aacc::g_device_error, &z, sizeof(unsigned));

@@ -261,61 +261,68 @@ class LLMTP:
         self.model.clear_all_slots()
         self._send({"action": "clear_all_slots"})
         staged = None
-        while self._loop_running or pending or active:
+        # Decode steps launched (and sent to the workers) but not read yet: (rows, read-back
+        # handle).  While the leader reads step t's tokens, step t+1 already runs on every rank.
+        inflight: list = []
+        while self._loop_running or pending or active or inflight:
             while True:
                 try:
                     pending.append(self._request_queue.get_nowait())
                 except queue.Empty:
                     break
-            if not pending and not active:
+            if not pending and not active and not inflight:
                 if not self._loop_running:
                     break
                 time.sleep(0.001)
                 continue
-            new_work = []
-            for req in list(pending):
-                while req.pending_indices and free_slots:
-                    new_work.append((req, req.pending_indices.pop(0), free_slots.pop(0)))
-                if not req.pending_indices:
-                    pending.remove(req)
-            if new_work:
-                seqs = [r.token_ids[i] for r, i, _ in new_work]
-                slots = [s for _, _, s in new_work]
-                temps = [r.temperature for r, _, _ in new_work]  # per request (the reference uses the first's)
-                seeds = [r.seeds[i] for r, i, _ in new_work]
-                self._send({"action": "prefill_flat", "sequences": seqs, "slots": slots, "temperatures": temps,
-                            "seeds": seeds})
-                toks = rt.prefill(seqs, slots, temperatures=temps, seeds=seeds).tolist()
-                released = []
-                for (req, idx, slot), tok in zip(new_work, toks):
-                    if 1 >= req.max_tokens or (not req.ignore_eos and tok == eos):
-                        self._finish(req, idx, [tok])
-                        kv.release(slot)
-                        released.append(slot)
-                        bisect.insort(free_slots, slot)
-                    else:
-                        active[slot] = [req, idx, [tok], len(req.token_ids[idx])]
-                if released:
-                    self._send({"action": "release", "slots": released})
-                staged = None
-            if not active:
-                continue
+            if not inflight:  # the batch only changes between steps that are all read
+                new_work = []
+                for req in list(pending):
+                    while req.pending_indices and free_slots:
+                        new_work.append((req, req.pending_indices.pop(0), free_slots.pop(0)))
+                    if not req.pending_indices:
+                        pending.remove(req)
+                if new_work:
+                    seqs = [r.token_ids[i] for r, i, _ in new_work]
+                    slots = [s for _, _, s in new_work]
+                    temps = [r.temperature for r, _, _ in new_work]  # per request (the reference uses the first's)
+                    seeds = [r.seeds[i] for r, i, _ in new_work]
+                    self._send({"action": "prefill_flat", "sequences": seqs, "slots": slots, "temperatures": temps,
+                                "seeds": seeds})
+                    toks = rt.prefill(seqs, slots, temperatures=temps, seeds=seeds).tolist()
+                    released = []
+                    for (req, idx, slot), tok in zip(new_work, toks):
+                        if 1 >= req.max_tokens or (not req.ignore_eos and tok == eos):
+                            self._finish(req, idx, [tok])
+                            kv.release(slot)
+                            released.append(slot)
+                            bisect.insort(free_slots, slot)
+                        else:
+                            active[slot] = [req, idx, [tok], len(req.token_ids[idx])]
+                    if released:
+                        self._send({"action": "release", "slots": released})
+                    staged = None
+                if not active:
+                    continue
             slots = list(active.keys())
-            B = len(slots)
-            restage = staged != slots
-            self._send({"action": "decode", "batch_size": B, "restage": restage, "slots": slots if restage else None})
-            if restage:
-                self._stage_decode([active[s][2][-1] for s in slots], [active[s][3] for s in slots], slots,
-                                   [active[s][0].temperature for s in slots],
-                                   [active[s][0].seeds[active[s][1]] for s in slots])
+            if not inflight:
+                inflight.append(self._launch_decode(rt, slots, staged != slots, active))
                 staged = slots
-            rt.decode_step(slots)
-            sampled = rt.read_tokens(B)
-            if self.tp_size > 1:  # a timed-out NVLink exchange leaves the group out of step: stop, do not crawl on
+            # Run one step ahead when that cannot change the batch (as LLM._run_loop does).
+            if (len(inflight) == 1 and inflight[0][0] == slots and not (pending and free_slots)
+                    and all(len(st[2]) + 1 < st[0].max_tokens and st[3] + 1 < self.max_seq_len
+                            for st in active.values())):
+                inflight.append(self._launch_decode(rt, slots, False, active))
+            step_slots, handle = inflight.pop(0)
+            sampled = rt.wait_tokens(handle, len(step_slots))
+            if self.tp_size > 1 and rt.token_error(handle):
+                # a timed-out NVLink exchange leaves the group out of step: stop, do not crawl on
                 _lib.raise_on_device_error("TP decode step")
             released = []
-            for slot, tok in zip(slots, sampled):
-                st = active[slot]
+            for slot, tok in zip(step_slots, sampled):
+                st = active.get(slot)
+                if st is None:  # ended at an earlier step; this token came from a step run ahead
+                    continue
                 st[2].append(tok)
                 st[3] += 1
                 req = st[0]
@@ -328,3 +335,15 @@ class LLMTP:
             if released:
                 self._send({"action": "release", "slots": released})
                 staged = None
+
+    def _launch_decode(self, rt, slots, restage, active):
+        """Send one decode step to the workers, stage it if the batch changed, run it
+        here and queue the read-back of its tokens."""
+        B = len(slots)
+        self._send({"action": "decode", "batch_size": B, "restage": restage, "slots": slots if restage else None})
+        if restage:
+            self._stage_decode([active[s][2][-1] for s in slots], [active[s][3] for s in slots], slots,
+                               [active[s][0].temperature for s in slots],
+                               [active[s][0].seeds[active[s][1]] for s in slots])
+        rt.decode_step(slots)
+        return slots, rt.copy_tokens_async(B)

@@ -78,6 +78,10 @@ def rope_table(max_pos: int, head_dim: int, theta: float, device, dtype=torch.bf
     return torch.cat([emb.cos().to(dtype)[:, :half], emb.sin().to(dtype)[:, :half]], dim=-1).contiguous()
 
 
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
 class PeerExchange:
     """NVLink exchange buffers of one TP group for aacc_tp_allreduce_add_rmsnorm.
 
@@ -231,6 +235,7 @@ class Qwen3Runtime:
         # two pinned read-back buffers, so a step's tokens can be read while the next step runs
         self._tok_ring = [torch.zeros(max_batch, dtype=torch.int64).pin_memory() for _ in range(2)]
         self._tok_events = [torch.cuda.Event(), torch.cuda.Event()]
+        self._tok_err = torch.zeros(2, dtype=torch.int32).pin_memory()  # device error word after each read-back
         self._tok_next = 0
         # TP: RowParallel outputs of decode-sized batches go over NVLink peer memory
         # (one fused kernel) instead of NCCL + separate residual/norm kernels.
@@ -489,6 +494,8 @@ class Qwen3Runtime:
         i = self._tok_next
         self._tok_next ^= 1
         self._tok_ring[i][:B].copy_(self.buf.ids[:B], non_blocking=True)
+        _lib.check(_lib.load().aacc_get_device_error_async(self._tok_err[i:].data_ptr(), _stream()),
+                   "aacc_get_device_error_async")
         self._tok_events[i].record()
         self.d2h_bytes += B * 8
         return i
@@ -497,6 +504,10 @@ class Qwen3Runtime:
         """Tokens of a copy_tokens_async call (waits for that copy only)."""
         self._tok_events[handle].synchronize()
         return self._tok_ring[handle][:B].tolist()
+
+    def token_error(self, handle: int) -> int:
+        """The device error word as it stood after that step (after wait_tokens)."""
+        return int(self._tok_err[handle])
 
     # ------------------------------------------------------------------ prefill
     def prefill(self, sequences: list[list[int]], rows: list[int], *, positions: list[list[int]] | None = None,

@@ -45,6 +45,10 @@ const char* aacc_last_error(void);
 unsigned long long aacc_launch_count(void);
 /* Copy the device error word of the current device into *out (synchronous). */
 int aacc_get_device_error(unsigned* out);
+/* The same read queued on `stream` behind its work (out: pinned host memory,
+ * valid once the stream reaches the copy), so an engine can check every step
+ * without waiting for the step queued after it. */
+int aacc_get_device_error_async(unsigned* out, cudaStream_t stream);
 int aacc_clear_device_error(void);
 
 /* ---- KV cache ------------------------------------------------------------ */

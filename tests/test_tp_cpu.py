@@ -216,6 +216,21 @@ def _engine_protocol(rank, world, n_req, slots, seed):
         def read_tokens(self, B):
             return self.buf.meta[0, :B].tolist()
 
+        snaps, unread, most_unread = [], 0, 0
+
+        def copy_tokens_async(self, B):
+            RT.snaps.append(self.buf.meta[0, :B].tolist())
+            RT.unread += 1
+            RT.most_unread = max(RT.most_unread, RT.unread)
+            return len(RT.snaps) - 1
+
+        def wait_tokens(self, handle, B):
+            RT.unread -= 1
+            return RT.snaps[handle][:B]
+
+        def token_error(self, handle):
+            return 0
+
     kv, rt = KV(), RT()
 
     class Model:
@@ -256,6 +271,8 @@ def _engine_protocol(rank, world, n_req, slots, seed):
     dist.all_gather_object(logs, log, group=D.get_tp_cpu_group())
     assert all(lg == logs[0] for lg in logs), "ranks ran different step sequences"
     assert any(e[0] == "decode" and e[1] != len([r for r in e[2] if r >= 0]) for e in logs[0])  # padded buckets ran
+    if rank == 0:
+        assert RT.most_unread == 2  # a step was run ahead while the previous one was read
 
 
 # ---------------------------------------------------------------------------- tests
