@@ -88,6 +88,8 @@ class LLM:
                  seed: int = 0, block_size: int = 256, use_cuda_graphs: bool = True,
                  prefill_chunk_tokens: int = 32768, device=None, verbose: bool = False):
         self.device = torch.device(device or "cuda")
+        if self.device.type == "cuda" and self.device.index is None:  # pin it: the loop runs in another thread
+            self.device = torch.device("cuda", torch.cuda.current_device())
         self.dtype = dtype
         self.max_seq_len = max_seq_len
         self.verbose = verbose
@@ -231,6 +233,8 @@ class LLM:
         active: dict[int, list] = {}
         pending: list[_Request] = []
         try:
+            if self.device.type == "cuda":  # a new thread starts on device 0: run on the engine's GPU
+                torch.cuda.set_device(self.device)
             self._run_loop(active, pending)
         except BaseException as e:  # noqa: BLE001 - propagate to every waiter
             self._loop_error = e

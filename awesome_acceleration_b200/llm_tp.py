@@ -219,6 +219,8 @@ class LLMTP:
     # ----------------------------------------------------------------- leader loop
     @torch.inference_mode()
     def _inference_loop(self):
+        if self.device.type == "cuda":  # a new thread starts on device 0: run on this rank's GPU
+            torch.cuda.set_device(self.device)
         if not self.is_tp_leader:
             self._worker_loop()
             return

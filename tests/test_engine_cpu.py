@@ -88,6 +88,7 @@ def _engine(slots, max_seq_len):
 
     eng = LLM.__new__(LLM)
     eng.model, eng.config = Model(), type("C", (), {"eos_token_id": EOS})()
+    eng.device = torch.device("cpu")
     eng.max_num_seqs, eng.max_seq_len, eng.tokenizer = slots, max_seq_len, None
     eng._request_queue, eng._loop_running, eng._loop_thread, eng._loop_error = queue.Queue(), False, None, None
     eng._base_seed, eng._serials = 0, itertools.count(1)
