@@ -186,11 +186,6 @@ def reset_job(llm, rows):
     llm.model.kv.clear_all()
 
 
-def count_launches(llm, B, out_tokens, n_prompts):
-    from awesome_acceleration_b200 import kernels as Kk
-    return Kk.LAUNCHES
-
-
 def run_cfg2(args, device):
     cfg2 = Cfg2(args)
     torch.manual_seed(0)
