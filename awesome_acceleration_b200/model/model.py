@@ -311,13 +311,17 @@ class Qwen3ForCausalLM(nn.Module):
         return model
 
     # ------------------------------------------------------------------ PD export/import
-    def export_request_kv(self, slot_idx: int, length: int) -> dict:
-        """Per-layer K/V of the first `length` tokens as CPU tensors [length, Hkv, 128]
-        (model/model.py:156-166, :386-390)."""
+    def export_request_kv(self, slot_idx: int, length: int, device="cpu") -> dict:
+        """Per-layer K/V of the first `length` tokens as tensors [length, Hkv, 128]
+        (model/model.py:156-166, :386-390).  On the CPU by default, as in the
+        reference; `device` may name another GPU instead, so that a prefill
+        engine hands a request to a decode engine in the same process over
+        NVLink (device-to-device copies of the gathered blocks) rather than
+        through host memory.  import_request_kv takes either."""
         out = []
         for i in range(self.config.num_hidden_layers):
             k, v = self.kv.gather(i, int(slot_idx), int(length))
-            out.append({"k": k.cpu(), "v": v.cpu(), "seqlen": int(self.kv.lengths[int(slot_idx)])})
+            out.append({"k": k.to(device), "v": v.to(device), "seqlen": int(self.kv.lengths[int(slot_idx)])})
         return {"layers": out}
 
     def import_request_kv(self, slot_idx: int, payload: dict, length: int):

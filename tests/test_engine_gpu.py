@@ -127,6 +127,13 @@ def test_export_import_request_kv(cuda):
         k0, v0 = m.kv.gather(s, 0, len(prompt))
         k3, v3 = m.kv.gather(s, 3, len(prompt))
         assert torch.equal(k0, k3) and torch.equal(v0, v3)
+    # device-resident hand-off (no host round trip): export to a GPU, import into slot 2
+    dev_payload = m.export_request_kv(0, len(prompt), device="cuda")
+    assert dev_payload["layers"][0]["k"].is_cuda
+    m.import_request_kv(2, dev_payload, len(prompt))
+    k2, v2 = m.kv.gather(1, 2, len(prompt))
+    k0, v0 = m.kv.gather(1, 0, len(prompt))
+    assert torch.equal(k0, k2) and torch.equal(v0, v2)
     outs = []
     for row in (0, 3):
         rt.load_decode_inputs(tok, [len(prompt)], [row])
