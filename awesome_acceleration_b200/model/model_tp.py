@@ -130,9 +130,13 @@ class Qwen3ForCausalLMTP(nn.Module):
         if self._lm_shard is not None:
             return
         w = self.model.embed_tokens.weight if self.lm_head is None else self.lm_head.weight
-        self._lm_shard = split_tensor_along_dim(w.data, self.tp_size, dim=0)
-        if self.lm_head is not None and self.tp_size > 1 and self._lm_shard.data_ptr() != w.data_ptr():
-            self.lm_head.weight.data = w.data.new_empty(0)  # untied: only this rank's shard is used from here on
+        shard = split_tensor_along_dim(w.data, self.tp_size, dim=0)  # a view into the full matrix
+        if self.lm_head is not None and self.tp_size > 1:
+            # untied: only this rank's shard is used from here on, so keep a copy of it and
+            # release the full matrix
+            shard = shard.clone()
+            self.lm_head.weight.data = w.data.new_empty(0)
+        self._lm_shard = shard
         self.runtime = None
 
     def init_kv_cache(self, num_slots: int, max_seq_len: int, device, dtype, *, block_size: int = 256,

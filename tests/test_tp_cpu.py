@@ -275,6 +275,37 @@ def _engine_protocol(rank, world, n_req, slots, seed):
         assert RT.most_unread == 2  # a step was run ahead while the previous one was read
 
 
+def _fused_weights_held_once(rank, world):
+    """After fuse_qkv a TP rank keeps one copy of its weights: the interleaved
+    gate/up (the separate gate/up released) and its own vocab shard of an
+    untied lm_head (the full matrix released)."""
+    import dataclasses
+    from awesome_acceleration_b200.model import distributed as D
+    from awesome_acceleration_b200.model.model import Qwen3Config
+    from awesome_acceleration_b200.model.model_tp import Qwen3ForCausalLMTP
+    from awesome_acceleration_b200.runtime import interleave_gate_up
+    from oracle.weights import TINY
+    D.init_distributed(world, backend="gloo", timeout_s=30)
+    arch = dataclasses.replace(TINY, tie_word_embeddings=False)
+    cfg = Qwen3Config(**{k: v for k, v in arch.as_dict().items() if k in Qwen3Config.__annotations__})
+    torch.manual_seed(0)
+    m = Qwen3ForCausalLMTP(cfg)
+    with torch.no_grad():
+        for prm in m.parameters():  # parallel layers allocate with torch.empty
+            prm.normal_()
+    full = m.lm_head.weight.detach().clone()
+    gates = [(l.mlp.gate_proj.weight.detach().clone(), l.mlp.up_proj.weight.detach().clone()) for l in m.model.layers]
+    m.fuse_qkv()
+    V = cfg.vocab_size // world
+    assert torch.equal(m._lm_shard, full[rank * V:(rank + 1) * V])
+    assert m.lm_head.weight.numel() == 0
+    for l, (g, u) in zip(m.model.layers, gates):
+        assert torch.equal(l.mlp._gate_up, interleave_gate_up(g, u))
+        assert l.mlp.gate_proj.weight.numel() == 0 and l.mlp.up_proj.weight.numel() == 0
+    m.fuse_qkv()  # a second call changes nothing
+    assert torch.equal(m._lm_shard, full[rank * V:(rank + 1) * V])
+
+
 # ---------------------------------------------------------------------------- tests
 @pytest.mark.parametrize("world,tp", [(2, 2), (4, 2), (4, 4)])
 def test_process_groups(world, tp):
@@ -310,4 +341,9 @@ def test_dead_worker_raises_instead_of_hanging():
 @pytest.mark.parametrize("world,n_req,slots", [(2, 40, 12), (3, 90, 40)])
 def test_llmtp_leader_worker_protocol(world, n_req, slots):
     res = spawn(world, _engine_protocol, n_req, slots, world * 1000 + n_req)
+    assert all(v is None for v in res.values()), res
+
+
+def test_fused_weights_held_once_on_tp_ranks():
+    res = spawn(2, _fused_weights_held_once)
     assert all(v is None for v in res.values()), res
