@@ -54,6 +54,7 @@ SIGNATURES: dict[str, tuple] = {
     "aacc_argmax_rows": (I32, [P, I64, I64, P, P]),
     "aacc_sample_rows": (I32, [P, I64, I64, P, P, P, P, P]),
     "aacc_argmax_merge": (I32, [P, P, I64, I32, P, P]),
+    "aacc_argmax_merge_strided": (I32, [P, P, I64, I32, I64, I64, P, P]),
     "aacc_tp_set_peer_wait_ms": (I32, [I64]),
     "aacc_tp_exchange_bytes": (I64, [I32, I64, I64]),
     "aacc_peer_buffer_alloc": (I32, [I64, P, P]),

@@ -66,15 +66,15 @@ __global__ void sample_rows_kernel(const bf16* __restrict__ logits, int64_t voca
   if (threadIdx.x == 0) tokens[m] = bi == INT64_MAX ? 0 : bi;
 }
 
+// Shard s's candidate of row m is (cv[s * sv + m], ci[s * si + m]).
 __global__ void argmax_merge_kernel(const float* __restrict__ cv, const int64_t* __restrict__ ci, int shards,
-                                    int64_t* __restrict__ tokens) {
+                                    int64_t sv, int64_t si, int64_t* __restrict__ tokens) {
   griddep_wait();
   griddep_launch();
   const int64_t m = blockIdx.x;
   float bv = -INFINITY;
   int64_t bi = INT64_MAX;
-  const int64_t M = gridDim.x;
-  for (int s = threadIdx.x; s < shards; s += blockDim.x) better(bv, bi, cv[s * M + m], ci[s * M + m]);
+  for (int s = threadIdx.x; s < shards; s += blockDim.x) better(bv, bi, cv[s * sv + m], ci[s * si + m]);
   block_argmax(bv, bi);
   if (threadIdx.x == 0) tokens[m] = bi == INT64_MAX ? 0 : bi;
 }
@@ -103,10 +103,17 @@ int aacc_sample_rows(const void* logits, int64_t M, int64_t vocab, const float* 
 
 int aacc_argmax_merge(const float* cand_val, const int64_t* cand_idx, int64_t M, int shards, int64_t* tokens,
                       cudaStream_t stream) {
-  if (M < 0 || shards <= 0) return set_error(AACC_ERR_INVALID, "argmax_merge: bad sizes");
+  return aacc_argmax_merge_strided(cand_val, cand_idx, M, shards, M, M, tokens, stream);
+}
+
+int aacc_argmax_merge_strided(const float* cand_val, const int64_t* cand_idx, int64_t M, int shards,
+                              int64_t val_shard_stride, int64_t idx_shard_stride, int64_t* tokens,
+                              cudaStream_t stream) {
+  if (M < 0 || shards <= 0 || val_shard_stride < M || idx_shard_stride < M)
+    return set_error(AACC_ERR_INVALID, "argmax_merge: bad sizes or shard strides");
   if (M == 0) return AACC_OK;
   return check_launch("argmax_merge", launch_k(argmax_merge_kernel, dim3((unsigned)M), dim3(32), 0, stream, cand_val,
-                                               cand_idx, shards, tokens));
+                                               cand_idx, shards, val_shard_stride, idx_shard_stride, tokens));
 }
 
 }  // extern "C"

@@ -268,6 +268,19 @@ def argmax_merge(cand_val, cand_idx, tokens=None):
     return tokens
 
 
+def argmax_merge_packed(gathered, M: int, tokens):
+    """Merge the vocab shards' candidates all-gathered as one int64 buffer
+    [shards, 2 M] per rank: ids in [:M], fp32 values in the first M float32
+    of [M:2M] (see Qwen3Runtime._argmax) -> tokens [M]."""
+    S, W = gathered.shape
+    if W != 2 * M or gathered.dtype != torch.int64 or not gathered.is_contiguous():
+        raise ValueError("argmax_merge_packed: expected a contiguous int64 [shards, 2 M] buffer")
+    vals = gathered.view(torch.float32)  # [S, 4 M]
+    _lib.check(_lib_().aacc_argmax_merge_strided(_p(vals[:, 2 * M:]), _p(gathered), M, S, 4 * M, 2 * M, _p(tokens),
+                                                 _stream()), "argmax_merge_packed")
+    return tokens
+
+
 def tp_set_peer_wait_ms(ms: int) -> None:
     """How long an exchange waits for a peer before it reports ERR_PEER_TIMEOUT (default 20 s)."""
     _lib.check(_lib_().aacc_tp_set_peer_wait_ms(int(ms)), "tp_set_peer_wait_ms")

@@ -194,9 +194,9 @@ class _DecodeBuffers:
         # split-K fp32 partials of the decode projections (the split count is
         # capped so that splits * B * N fits): 32 MB
         self.part = torch.empty(max(8 << 20, 16 * B * H), dtype=torch.float32, device=device)
-        if tp > 1:  # all-gathered argmax candidates, viewed as [tp, batch] per step
-            self.g_best = torch.zeros(tp * B, dtype=torch.float32, device=device)
-            self.g_tok = torch.zeros(tp * B, **i64)
+        if tp > 1:  # this rank's argmax candidates (ids | fp32 scores) and the all-gathered [tp, 2 B]
+            self.cand = torch.zeros(2 * B, **i64)
+            self.g_cand = torch.zeros(tp * 2 * B, **i64)
 
 
 class Qwen3Runtime:
@@ -313,18 +313,23 @@ class Qwen3Runtime:
             nxt = self.layers[i + 1].in_ln if i + 1 < L else self.final_norm
             self._row_parallel(act, lw.wd, delta, res, nxt, x, part)
 
-    def _argmax(self, x, tokens, best, ws, logits=None, g_best=None, g_tok=None, sample=None):
+    def _argmax(self, x, tokens, best, ws, logits=None, cand=None, gathered=None, sample=None):
         """Next token of each row of x (greedy, or sampled for rows whose
-        temperature in `sample` = (temperature, seeds, counters) is > 0);
-        under TP every rank scores its vocab shard and the (score, id)
-        candidates are all-gathered and merged."""
+        temperature in `sample` = (temperature, seeds, counters) is > 0).
+        Under TP every rank scores its vocab shard into `cand` (int64 [2 M]:
+        global ids in [:M], fp32 scores in the first M float32 of [M:]), ONE
+        all-gather collects every rank's candidates into `gathered`
+        ([tp, 2 M]) and the merge kernel picks the best (lowest id on ties)."""
         t, sd, ct = sample if sample is not None else (None, None, None)
-        K.lm_head_argmax(x, self.lm_head, tokens, ws, logits=logits, best_val=best, vocab_offset=self.vocab_offset,
-                         temperature=t, seeds=sd, counters=ct)
-        if self.comm.size > 1:
-            self.comm.all_gather(g_best, best)
-            self.comm.all_gather(g_tok, tokens)
-            K.argmax_merge(g_best, g_tok, tokens)
+        if self.comm.size == 1:
+            K.lm_head_argmax(x, self.lm_head, tokens, ws, logits=logits, best_val=best,
+                             vocab_offset=self.vocab_offset, temperature=t, seeds=sd, counters=ct)
+            return
+        M = x.shape[0]
+        K.lm_head_argmax(x, self.lm_head, cand[:M], ws, logits=logits, best_val=cand[M:].view(torch.float32)[:M],
+                         vocab_offset=self.vocab_offset, temperature=t, seeds=sd, counters=ct)
+        self.comm.all_gather(gathered, cand)
+        K.argmax_merge_packed(gathered, M, tokens)
 
     # ------------------------------------------------------------------ decode
     def _decode_body(self, B: int, logits=None):
@@ -341,10 +346,10 @@ class Qwen3Runtime:
         self._layer_chain(b.x[:B], b.res[:B], b.delta[:B], b.q[:B], b.attn[:B], b.act[:B], attend, pos,
                           b.slot_map[:B], part=b.part)
         t = self.comm.size
-        g_best = b.g_best[:t * B].view(t, B) if t > 1 else None
-        g_tok = b.g_tok[:t * B].view(t, B) if t > 1 else None
+        cand = b.cand[:2 * B] if t > 1 else None
+        gathered = b.g_cand[:t * 2 * B].view(t, 2 * B) if t > 1 else None
         # sampling counter = position of the input token (advances on device every step)
-        self._argmax(b.x[:B], ids, b.best[:B], b.lm_ws, logits=logits, g_best=g_best, g_tok=g_tok,
+        self._argmax(b.x[:B], ids, b.best[:B], b.lm_ws, logits=logits, cand=cand, gathered=gathered,
                      sample=(b.temp[:B], b.seed[:B], pos))
         K.advance_seqlens(rows, kv.seqlens, pos)
 
@@ -620,9 +625,9 @@ class Qwen3Runtime:
                 lg = out_logits[a:a + m] if last_logits else None
                 sm = None if samp is None else tuple(t[a:a + m] for t in samp)
                 if self.comm.size > 1:
-                    gb = torch.empty((self.comm.size, m), dtype=torch.float32, device=dev)
-                    gt = torch.empty((self.comm.size, m), dtype=torch.int64, device=dev)
-                    self._argmax(hx, tokens[a:a + m], best[a:a + m], lm_ws, logits=lg, g_best=gb, g_tok=gt,
+                    cand = torch.empty(2 * m, dtype=torch.int64, device=dev)
+                    gathered = torch.empty((self.comm.size, 2 * m), dtype=torch.int64, device=dev)
+                    self._argmax(hx, tokens[a:a + m], best[a:a + m], lm_ws, logits=lg, cand=cand, gathered=gathered,
                                  sample=sm)
                 else:
                     self._argmax(hx, tokens[a:a + m], best[a:a + m], lm_ws, logits=lg, sample=sm)

@@ -275,6 +275,15 @@ int aacc_argmax_rows(const void* logits, int64_t M, int64_t vocab, int64_t* toke
 int aacc_argmax_merge(const float* cand_val, const int64_t* cand_idx, int64_t M, int shards,
                       int64_t* tokens, cudaStream_t stream);
 
+/* The same merge over candidates laid out with a per-shard stride (in
+ * elements): shard s's value of row m is cand_val[s * val_shard_stride + m],
+ * its id cand_idx[s * idx_shard_stride + m].  Lets a TP group all-gather each
+ * rank's (ids, values) as ONE packed buffer and merge in place (the
+ * reference gathers full logits to rank 0 instead, model/model_tp.py:369-381). */
+int aacc_argmax_merge_strided(const float* cand_val, const int64_t* cand_idx, int64_t M, int shards,
+                              int64_t val_shard_stride, int64_t idx_shard_stride, int64_t* tokens,
+                              cudaStream_t stream);
+
 /* ---- tensor-parallel exchange over NVLink peer memory -------------------- */
 
 /* Bytes of the exchange buffer each rank of a TP group allocates for

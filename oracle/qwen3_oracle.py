@@ -168,26 +168,43 @@ class Qwen3Oracle:
         cos, sin = rope_cos_sin(pos, a.head_dim, a.rope_theta, self.dtype)
         cos, sin = cos.unsqueeze(1), sin.unsqueeze(1)
         hidden = self.w["model.embed_tokens.weight"][ids]
-        B = len(tokens)
         for i in range(a.num_hidden_layers):
-            residual = hidden
-            h = rms_norm(hidden, self._lw(i, "input_layernorm.weight"), eps)
-            q, k, v = self._qkv(i, h)
-            q, k = apply_rope(q, k, cos, sin)
-            o = torch.empty_like(q)
-            for b, slot in enumerate(slots):
-                n = int(self.seqlens[slot])
-                self.k_cache[i][slot, n] = k[b]
-                self.v_cache[i][slot, n] = v[b]
-                o[b] = fa.attend(q[b:b + 1], self.k_cache[i][slot, :n + 1],
-                                 self.v_cache[i][slot, :n + 1], self.scaling, False)[0]
-            hidden = residual + F.linear(o.reshape(B, -1), self._lw(i, "self_attn.o_proj.weight"))
-            residual = hidden
-            h = rms_norm(hidden, self._lw(i, "post_attention_layernorm.weight"), eps)
-            hidden = residual + self._mlp(i, h)
+            hidden = self.decode_layer(i, hidden, cos, sin, slots)
         for slot in slots:
             self.seqlens[slot] += 1
         return rms_norm(hidden, self.w["model.norm.weight"], eps)
+
+    def rope_rows(self, positions: list[int]):
+        """cos / sin of the decode positions, shaped to broadcast over heads."""
+        pos = torch.tensor(positions, dtype=torch.long, device=self.device)
+        cos, sin = rope_cos_sin(pos, self.arch.head_dim, self.arch.rope_theta, self.dtype)
+        return cos.unsqueeze(1), sin.unsqueeze(1)
+
+    def decode_layer(self, i: int, hidden: torch.Tensor, cos, sin, slots: list[int]) -> torch.Tensor:
+        """TransformerBlock i on one decode token per row (model/model.py:202-267,
+        decode branch :231-241): the new K/V go to position seqlens[slot]
+        (not advanced here) and the token attends over seqlens[slot] + 1."""
+        eps = self.arch.rms_norm_eps
+        B = hidden.shape[0]
+        residual = hidden
+        h = rms_norm(hidden, self._lw(i, "input_layernorm.weight"), eps)
+        q, k, v = self._qkv(i, h)
+        q, k = apply_rope(q, k, cos, sin)
+        o = torch.empty_like(q)
+        for b, slot in enumerate(slots):
+            n = int(self.seqlens[slot])
+            self.k_cache[i][slot, n] = k[b]
+            self.v_cache[i][slot, n] = v[b]
+            o[b] = fa.attend(q[b:b + 1], self.k_cache[i][slot, :n + 1],
+                             self.v_cache[i][slot, :n + 1], self.scaling, False)[0]
+        hidden = residual + F.linear(o.reshape(B, -1), self._lw(i, "self_attn.o_proj.weight"))
+        residual = hidden
+        h = rms_norm(hidden, self._lw(i, "post_attention_layernorm.weight"), eps)
+        return residual + self._mlp(i, h)
+
+    def head(self, hidden: torch.Tensor) -> torch.Tensor:
+        """Final norm + lm_head (model/model.py:285-286, :316-318) -> logits."""
+        return F.linear(rms_norm(hidden, self.w["model.norm.weight"], self.arch.rms_norm_eps), self.lm_head)
 
     def decode(self, tokens: list[int], positions: list[int], slots: list[int]) -> torch.Tensor:
         """One decode step -> logits [B, V] (llm.py:210-213)."""

@@ -48,6 +48,9 @@ TINY = Qwen3Arch(vocab_size=4096, hidden_size=256, intermediate_size=512, num_hi
                  num_attention_heads=4, num_key_value_heads=2)
 TINY_G4 = Qwen3Arch(vocab_size=3000, hidden_size=512, intermediate_size=768, num_hidden_layers=2,
                     num_attention_heads=8, num_key_value_heads=2)
+# Qwen3-8B layer shapes and vocabulary with two layers (tensor-parallel parity case).
+TP8B_2L = Qwen3Arch(hidden_size=4096, intermediate_size=12288, num_hidden_layers=2, num_attention_heads=32,
+                    num_key_value_heads=8, tie_word_embeddings=False)
 
 
 def init_weights(arch: Qwen3Arch, seed: int, std: float = 0.02, norm_jitter: float = 0.0,

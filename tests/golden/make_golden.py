@@ -30,7 +30,7 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 
 from oracle import attention as fa  # noqa: E402
-from oracle.weights import QWEN3_0_6B, TINY, TINY_G4, init_weights, random_prompts  # noqa: E402
+from oracle.weights import QWEN3_0_6B, TINY, TINY_G4, TP8B_2L, init_weights, random_prompts  # noqa: E402
 
 # name: (arch, dtype, seed, norm_jitter, prompt lengths, decode steps, kv layers, kv positions)
 CASES = {
@@ -39,6 +39,12 @@ CASES = {
     "tiny_fp32_ragged": (TINY, torch.float32, 7, 0.1, [5, 17, 40, 1], 8, [0, 1], [0, 4, 16, 39, 47]),
     "tiny_bf16_ragged": (TINY, torch.bfloat16, 7, 0.1, [5, 17, 40, 1], 8, [0, 1], [0, 4, 16, 39, 47]),
     "tinyg4_bf16": (TINY_G4, torch.bfloat16, 11, 0.1, [33, 300], 6, [0, 1], [0, 255, 256, 299, 305]),
+    # Qwen3-0.6B in bf16 at the engine's dtype: 4 x 128 prompt tokens, 64 greedy decode steps.
+    "qwen06b_bf16_64": (QWEN3_0_6B, torch.bfloat16, 2024, 0.0, [128] * 4, 64, [0, 27],
+                        [0, 127, 128, 191]),
+    # Qwen3-8B proportions (hidden 4096, 32 / 8 heads, MLP 12288, untied lm_head), two layers:
+    # the tensor-parallel parity case (G = 4 query heads per kv head on every rank at TP 2 / 4).
+    "tp8b2l_bf16": (TP8B_2L, torch.bfloat16, 31, 0.1, [96, 33, 128, 7], 32, [0, 1], [0, 6, 32, 95, 127, 150]),
 }
 N_SUB = 512
 

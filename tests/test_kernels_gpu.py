@@ -388,6 +388,12 @@ def test_argmax_merge_ties_lowest_index(cuda):
     idx = torch.tensor([[10, 7], [20, 3], [5, 1]], dtype=torch.int64, device=cuda)
     out = K().argmax_merge(val, idx)
     assert out.tolist() == [5, 3]
+    # the TP path's packed layout: one int64 buffer per shard, ids | fp32 values
+    S, M = val.shape
+    packed = torch.zeros((S, 2 * M), dtype=torch.int64, device=cuda)
+    packed[:, :M] = idx
+    packed.view(torch.float32)[:, 2 * M:3 * M] = val
+    assert K().argmax_merge_packed(packed, M, torch.empty(M, dtype=torch.int64, device=cuda)).tolist() == [5, 3]
 
 
 @pytest.mark.parametrize("M,V", [(300, 1000), (64, 151936)])

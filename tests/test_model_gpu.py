@@ -4,7 +4,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import load_golden
+from conftest import build_model, load_golden
 from oracle.qwen3_oracle import Qwen3Oracle, run_greedy
 from oracle.weights import TINY, Qwen3Arch, init_weights, random_prompts
 
@@ -17,21 +17,6 @@ TOL = 2e-2  # logits max-abs, bf16
 # is bf16 accumulation order, not an algorithmic difference.  The full-size
 # goldens are therefore checked at 2.5 bf16 ulps of the largest logit.
 TOL_BY_CASE = {"cfg1_0p6b_bf16_short": 4e-2}
-
-
-def build_model(arch: Qwen3Arch, sd: dict, num_slots: int, max_seq_len: int, dev, **kw):
-    from awesome_acceleration_b200.model.model import Qwen3Config, Qwen3ForCausalLM
-    cfg = Qwen3Config(**{k: v for k, v in arch.as_dict().items() if k in Qwen3Config.__annotations__})
-    with torch.device("meta"):
-        m = Qwen3ForCausalLM(cfg)
-    m = m.to_empty(device=dev).to(torch.bfloat16)
-    missing, unexpected = m.load_state_dict({k: v.to(torch.bfloat16) for k, v in sd.items()}, strict=False)
-    assert not unexpected
-    for k, v in kw.items():
-        setattr(m, k, v)
-    m.fuse_qkv()
-    m.init_kv_cache(num_slots, max_seq_len, dev, torch.bfloat16, block_size=kw.get("block_size", 256))
-    return m
 
 
 def check_step(step, lg_mine, toks_mine, g, tol=TOL):

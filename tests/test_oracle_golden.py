@@ -8,7 +8,8 @@ from conftest import load_golden
 from oracle.qwen3_oracle import Qwen3Oracle
 from oracle.weights import Qwen3Arch, init_weights
 
-CASES = ["tiny_fp32_ragged", "tiny_bf16_ragged", "tinyg4_bf16", "cfg1_0p6b_bf16_short", "cfg1_0p6b_fp32"]
+CASES = ["tiny_fp32_ragged", "tiny_bf16_ragged", "tinyg4_bf16", "cfg1_0p6b_bf16_short", "cfg1_0p6b_fp32",
+         "qwen06b_bf16_64", "tp8b2l_bf16"]
 
 
 def run_oracle_on_golden(g: dict):
@@ -69,3 +70,23 @@ def test_paged_slot_restatement():
     perm = rng.permutation(nslots * per).reshape(nslots, per)
     seen = {paged_slot(perm[s], p, bs) for s in range(nslots) for p in range(max_seq_len)}
     assert len(seen) == nslots * max_seq_len
+
+
+@pytest.mark.parametrize("name", ["qwen06b_bf16_64", "tp8b2l_bf16"])
+def test_reference_cross_device_spread(name):
+    """The committed cuBLAS run of the reference path (make_gpu_reference.py,
+    teacher-forced with the CPU golden's tokens) against the reference's own
+    CPU run: the same computation on two devices differs by a few bf16 ulps of
+    the row's largest logit at every step, which is why the B200 path's
+    end-to-end logits are held to this spread (and each op to 2e-2)."""
+    from conftest import bf16_ulp, load_gpuref
+    g, r = load_golden(name), load_gpuref(name)
+    assert r is not None, f"{name}_gpuref.npz missing"
+    assert r["logits_sub"].shape == g["logits_sub"].shape
+    err = np.abs(r["logits_sub"] - g["logits_sub"])
+    row_ulp = bf16_ulp(np.abs(g["logits_sub"]).max(axis=2, keepdims=True))
+    print(f"{name}: cuBLAS vs CPU reference logits max-abs {err.max():.4f}, rms {np.sqrt((err ** 2).mean()):.4f}, "
+          f"{(err / row_ulp).max():.1f} ulps of the row maximum; greedy top-1 agreement "
+          f"{(r['top2_idx'][..., 0] == g['top2_idx'][..., 0]).mean():.3f}")
+    assert 0.02 < err.max() < 0.1  # recorded spread (bf16 drift, not a different algorithm)
+    assert (r["top2_idx"][..., 0] == g["top2_idx"][..., 0]).mean() >= 0.95

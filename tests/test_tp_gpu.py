@@ -1,5 +1,7 @@
-"""Tensor parallelism on >= 2 GPUs (NCCL): the TP model and the LLMTP
-leader/worker engine against the single-GPU path on the same weights."""
+"""Tensor parallelism on >= 2 GPUs (NCCL + the NVLink exchange): the TP model
+against the reference's golden vectors (Qwen3-8B layer shapes, two layers,
+tests/golden/tp8b2l_bf16.npz) at TP = 2 / 4 / 8, the LLMTP leader/worker
+engine, and the exchange kernel against an exact rank-order sum."""
 import os
 import socket
 import traceback
@@ -63,77 +65,78 @@ def _prompts():
     return [p[:n] for p, n in zip(random_prompts(4, 90, TINY.vocab_size, 31), [90, 7, 40, 64])]
 
 
-def _tp_model_stream(rank, world, steps):
-    """Prefill + decode on the TP model; returns tokens and last-step logits."""
+def _tp_golden_case(rank, world):
+    """One rank of the TP model on the 8B-shaped golden: teacher-forced
+    logits (shards gathered) at every step, then the free-running greedy
+    stream through the captured decode graphs (RowParallel outputs over the
+    NVLink exchange, vocab-parallel argmax)."""
     import sys
-    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path[:0] = [os.path.dirname(here), here]
+    import numpy as np
+    from conftest import load_golden
+    from test_parity_gpu import free_running
+    from awesome_acceleration_b200 import _lib
     from awesome_acceleration_b200.model import distributed as D
     from awesome_acceleration_b200.model.model import Qwen3Config
     from awesome_acceleration_b200.model.model_tp import Qwen3ForCausalLMTP
-    from oracle.weights import TINY, init_weights
-    D.init_distributed(world, timeout_s=120)
+    from oracle.weights import Qwen3Arch, init_weights
+    D.init_distributed(world, timeout_s=300)
     dev = torch.device("cuda", rank)
-    cfg = Qwen3Config(**{k: v for k, v in TINY.as_dict().items() if k in Qwen3Config.__annotations__})
-    sd = init_weights(TINY, 30, norm_jitter=0.1)
+    g = load_golden("tp8b2l_bf16")
+    arch = Qwen3Arch(**g["arch"])
+    cfg = Qwen3Config(**{k: v for k, v in arch.as_dict().items() if k in Qwen3Config.__annotations__})
+    sd = init_weights(arch, int(g["seed"]), norm_jitter=float(g["norm_jitter"]))
     m = Qwen3ForCausalLMTP.from_state_dict(sd, cfg, dev)
+    del sd
     m.fuse_qkv()
-    m.init_kv_cache(4, 256, dev, torch.bfloat16)
+    lens = g["lens"].tolist()
+    prompts = [g["prompts"][i][:L].tolist() for i, L in enumerate(lens)]
+    slots = g["slots"].tolist()
+    m.init_kv_cache(len(lens), int(g["max_seq_len"]), dev, torch.bfloat16)
     rt = m._rt()
-    prompts = _prompts()
-    rows = [0, 1, 2, 3]
-    toks = rt.prefill(prompts, rows).tolist()
-    seq = [toks]
-    rt.load_decode_inputs(toks, [len(p) for p in prompts], rows)
-    for _ in range(steps):
-        rt.decode_step(rows)
-        seq.append(rt.read_tokens(4))
-    # one more step with materialised (gathered) logits through forward()
-    ids = torch.tensor([[t] for t in seq[-1]], device=dev)
-    pos = torch.tensor([[len(p) + steps] for p in prompts], device=dev)
-    logits = m(ids, pos, torch.tensor(rows, device=dev))[:, 0].float().cpu()
-    return seq, logits
+    vi = torch.from_numpy(g["vocab_idx"]).to(dev)
+
+    def full(shard):
+        return D.tensor_model_parallel_all_gather(shard.contiguous(), dim=-1)
+
+    _, lg = rt.prefill(prompts, slots, last_logits=True)
+    subs = [full(lg).float()[:, vi].cpu().numpy()]
+    pos = list(lens)
+    for s in range(int(g["steps"])):
+        rt.load_decode_inputs(g["tokens"][:, s].tolist(), pos, slots)
+        shard = torch.empty((len(slots), rt.vocab_local), dtype=torch.bfloat16, device=dev)
+        rt.decode_step(slots, logits=shard)
+        subs.append(full(shard).float()[:, vi].cpu().numpy())
+        pos = [p + 1 for p in pos]
+    mine = np.stack(subs)
+    m.kv.clear_all()
+    near = free_running(m, g, prompts, lens, slots)
+    exchange = rt.comm.exchange is not None
+    assert _lib.device_error() == 0
+    err = np.abs(mine - g["logits_sub"])
+    return float(err.max()), float(np.sqrt((err ** 2).mean())), int((err <= 2e-2).sum()), err.size, near, exchange
 
 
-def _single_stream(steps):
-    from awesome_acceleration_b200.model.model import Qwen3Config, Qwen3ForCausalLM
-    from oracle.weights import TINY, init_weights
-    dev = torch.device("cuda", 0)
-    cfg = Qwen3Config(**{k: v for k, v in TINY.as_dict().items() if k in Qwen3Config.__annotations__})
-    sd = init_weights(TINY, 30, norm_jitter=0.1)
-    with torch.device("meta"):
-        m = Qwen3ForCausalLM(cfg)
-    m = m.to_empty(device=dev).to(torch.bfloat16)
-    m.load_state_dict({k: v.to(torch.bfloat16) for k, v in sd.items()}, strict=False)
-    m.fuse_qkv()
-    m.init_kv_cache(4, 256, dev, torch.bfloat16)
-    rt = m._rt()
-    prompts = _prompts()
-    rows = [0, 1, 2, 3]
-    toks = rt.prefill(prompts, rows).tolist()
-    seq = [toks]
-    rt.load_decode_inputs(toks, [len(p) for p in prompts], rows)
-    for _ in range(steps):
-        rt.decode_step(rows)
-        seq.append(rt.read_tokens(4))
-    ids = torch.tensor([[t] for t in seq[-1]], device=dev)
-    pos = torch.tensor([[len(p) + steps] for p in prompts], device=dev)
-    logits = m(ids, pos, torch.tensor(rows, device=dev))[:, 0].float().cpu()
-    return seq, logits
-
-
-@pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
-def test_tp2_matches_single_gpu(cuda):
-    steps = 12
-    tp = run_ranks(2, _tp_model_stream, steps)
-    assert tp[0][0] == tp[1][0], "TP ranks disagree on the greedy stream"
-    assert torch.equal(tp[0][1], tp[1][1]), "TP ranks disagree on the gathered logits"
-    single_seq, single_logits = _single_stream(steps)
-    err = (tp[0][1] - single_logits).abs().max().item()
-    assert err <= 2e-2, f"TP=2 logits differ from TP=1 by {err}"
-    # Greedy streams agree until a near-tie (the all-reduce sums partial
-    # products in a different order than the single-GPU GEMM).
-    same = sum(a == b for a, b in zip(tp[0][0], single_seq))
-    assert same >= len(single_seq) // 2, (tp[0][0], single_seq)
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_vs_reference_golden(cuda, world):
+    """TP = world on the Qwen3-8B layer shapes (32 / 8 heads: 4 query heads per
+    kv head on every rank, hidden 4096, untied vocab-parallel lm_head): logits
+    within the reference's own CPU-vs-cuBLAS spread at every step, and the
+    free-running greedy stream equal to the reference's except at its near-ties."""
+    if _ngpu() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from test_parity_gpu import SPREAD_MARGIN, TOL, reference_spread
+    res = run_ranks(world, _tp_golden_case, timeout=900)
+    ref_mx, ref_rms = reference_spread("tp8b2l_bf16")
+    mx, rms, within, total, near, exchange = res[0]
+    for r in range(1, world):
+        assert res[r][4] == near, f"rank {r} saw a different greedy stream"
+    print(f"\nTP={world} (NVLink exchange: {exchange}): logits max-abs {mx:.4f}, rms {rms:.4f} (reference's own "
+          f"spread {ref_mx:.4f} / {ref_rms:.4f}); {within} of {total} logits within {TOL}; "
+          f"{len(near)} reference near-tie steps {near}")
+    assert exchange, "the NVLink exchange was not set up"
+    assert mx <= max(TOL, SPREAD_MARGIN * ref_mx) and rms <= SPREAD_MARGIN * ref_rms
 
 
 def _llmtp_engine(rank, world):
