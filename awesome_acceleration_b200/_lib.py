@@ -42,6 +42,8 @@ SIGNATURES: dict[str, tuple] = {
     "aacc_gemm": (I32, [P, P, P, I64, I64, I64, P]),
     "aacc_gemm_silu_mul": (I32, [P, P, P, I64, I64, I64, P]),
     "aacc_gemm_splitk": (I32, [P, P, P, I64, I64, I64, I32, P]),
+    "aacc_gemm_bias": (I32, [P, P, P, P, I64, I64, I64, P]),
+    "aacc_bias_add": (I32, [P, P, I64, I64, P]),
     "aacc_splitk_add_rmsnorm": (I32, [P, I32, P, P, P, I64, I64, F32, P]),
     "aacc_splitk_reduce": (I32, [P, I32, P, I64, I64, P]),
     "aacc_splitk_qkv_norm_rope_store": (I32, [P, I32, P, P, F32, P, P, I64, P, P, P, P, I64, I32, I32, I32, I64,

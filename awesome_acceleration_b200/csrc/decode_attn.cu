@@ -300,6 +300,23 @@ static int default_split(int64_t batch, int Hkv, int64_t max_ctx) {
 
 static size_t decode_smem_bytes() { return sizeof(DecodeSmem) + 1024; }
 
+// Argument checks shared by both decode-attention entry points; they run
+// before either one touches the device or the stream.
+static int decode_check(const char* what, int64_t batch, int64_t num_blocks, int64_t max_blocks, int num_q_heads,
+                        int num_kv_heads, int block_size, int64_t max_context, int split_tokens) {
+  if (batch < 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads || block_size <= 0 ||
+      block_size % kTile || num_blocks <= 0 || max_blocks <= 0 || max_context <= 0)
+    return set_error(AACC_ERR_INVALID, "%s: bad sizes", what);
+  const int G = num_q_heads / num_kv_heads;
+  if (G != 1 && G != 2 && G != 4 && G != 8)
+    return set_error(AACC_ERR_UNSUPPORTED, "%s: q/kv head ratio %d not in {1,2,4,8}", what, G);
+  if (num_blocks * num_kv_heads * block_size >= (int64_t(1) << 31))
+    return set_error(AACC_ERR_UNSUPPORTED, "%s: pool too large", what);
+  if (split_tokens > 0 && split_tokens % kTile)
+    return set_error(AACC_ERR_INVALID, "%s: split_tokens must be a multiple of %d", what, kTile);
+  return AACC_OK;
+}
+
 }  // namespace aacc
 
 using namespace aacc;
@@ -321,18 +338,13 @@ int aacc_paged_decode_attention(const void* q, void* out, const void* k_cache, c
                                 int num_kv_heads, int block_size, float scale, int split_tokens,
                                 int64_t max_context, void* workspace, int64_t workspace_bytes,
                                 cudaStream_t stream) {
-  if (batch < 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads || block_size <= 0 || block_size % kTile ||
-      num_blocks <= 0 || max_blocks <= 0 || max_context <= 0)
-    return set_error(AACC_ERR_INVALID, "paged_decode_attention: bad sizes");
-  if (batch == 0) return AACC_OK;
+  int st = decode_check("paged_decode_attention", batch, num_blocks, max_blocks, num_q_heads, num_kv_heads,
+                        block_size, max_context, split_tokens);
+  if (st || batch == 0) return st;
   const int G = num_q_heads / num_kv_heads;
-  if (G != 1 && G != 2 && G != 4 && G != 8)
-    return set_error(AACC_ERR_UNSUPPORTED, "paged_decode_attention: q/kv head ratio %d not in {1,2,4,8}", G);
   if (max_context > max_blocks * block_size) max_context = max_blocks * block_size;
   const int64_t rows = num_blocks * num_kv_heads * block_size;
-  if (rows >= (int64_t(1) << 31)) return set_error(AACC_ERR_UNSUPPORTED, "paged_decode_attention: pool too large");
   if (split_tokens <= 0) split_tokens = default_split(batch, num_kv_heads, max_context);
-  if (split_tokens % kTile) return set_error(AACC_ERR_INVALID, "split_tokens must be a multiple of %d", kTile);
   const int max_splits = (int)((max_context + split_tokens - 1) / split_tokens);
   if (max_splits > 1) {
     const int64_t need = batch * num_q_heads * (int64_t)max_splits * (kD + 2) * (int64_t)sizeof(float) +
@@ -342,7 +354,7 @@ int aacc_paged_decode_attention(const void* q, void* out, const void* k_cache, c
                        (long long)workspace_bytes, (long long)need);
   }
   CUtensorMap tmk, tmv;
-  int st = make_tmap_2d(&tmk, k_cache, kD, rows, kD * 2, 64, kTile, true);
+  st = make_tmap_2d(&tmk, k_cache, kD, rows, kD * 2, 64, kTile, true);
   if (st) return st;
   st = make_tmap_2d(&tmv, v_cache, kD, rows, kD * 2, 64, kTile, true);
   if (st) return st;
@@ -428,14 +440,14 @@ int aacc_paged_decode_attention_noalloc(const void* q, void* out, const void* k_
                                         const int64_t* slot_indices, const int32_t* seqlens, int ctx_add,
                                         int64_t batch, int num_q_heads, int num_kv_heads, int block_size,
                                         float scale, int split_tokens, int64_t max_context, cudaStream_t stream) {
-  if (batch < 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads || block_size <= 0 ||
-      max_blocks <= 0 || max_context <= 0)
-    return set_error(AACC_ERR_INVALID, "paged_decode_attention_noalloc: bad sizes");
-  if (batch == 0) return AACC_OK;
+  // Every argument check comes before the scratch lookup and the counter
+  // clear, so a rejected call leaves nothing on the caller's stream.
+  int st = decode_check("paged_decode_attention_noalloc", batch, num_blocks, max_blocks, num_q_heads, num_kv_heads,
+                        block_size, max_context, split_tokens);
+  if (st || batch == 0) return st;
   // The same split plan as aacc_paged_decode_attention, to size the scratch.
   int64_t ctx = max_context > max_blocks * block_size ? max_blocks * block_size : max_context;
   const int split = split_tokens > 0 ? split_tokens : default_split(batch, num_kv_heads, ctx);
-  if (split % kTile) return set_error(AACC_ERR_INVALID, "split_tokens must be a multiple of %d", kTile);
   const int64_t max_splits = (ctx + split - 1) / split;
   const int64_t partial_bytes = batch * num_q_heads * max_splits * (kD + 2) * (int64_t)sizeof(float);
   const int64_t counter_bytes = batch * num_kv_heads * (int64_t)sizeof(int);
@@ -447,7 +459,7 @@ int aacc_paged_decode_attention_noalloc(const void* q, void* out, const void* k_
                      (long long)batch, num_q_heads, (long long)max_splits,
                      (long long)(partial_bytes + counter_bytes), (long long)kNoAllocScratchBytes);
   void* scratch = nullptr;
-  int st = noalloc_scratch(&scratch);
+  st = noalloc_scratch(&scratch);
   if (st) return st;
   if (max_splits > 1) {
     cudaError_t e = cudaMemsetAsync(static_cast<char*>(scratch) + partial_bytes, 0, counter_bytes, stream);

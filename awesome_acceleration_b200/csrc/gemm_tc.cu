@@ -34,6 +34,7 @@ enum Epi { EPI_STORE = 0, EPI_SILU = 1, EPI_QKV = 2, EPI_ARGMAX = 3, EPI_PARTIAL
 struct EpiParams {
   bf16* out;
   int64_t ldo;
+  const bf16* bias;  // EPI_STORE: optional per-column bias [N], added in fp32 before the bf16 rounding
   // EPI_PARTIAL (split-K): fp32 partial sums part[split][M][N]
   float* part;
   int64_t part_rows;  // M
@@ -152,6 +153,11 @@ __device__ __forceinline__ void epilogue_group(uint32_t tcol, int64_t m, bool ro
     for (int c = 0; c < 128; c += 16) {
       float v[16];
       tmem_ld16(tcol + c, v);
+      if (p.bias) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (n0 + c + i < N) v[i] += bf(p.bias[n0 + c + i]);
+      }
       if (row_ok) {
         if (n0 + c + 16 <= N) {
           store16_bf16(p.out + m * p.ldo + n0 + c, v);
@@ -544,6 +550,19 @@ int aacc_gemm(const void* x, const void* w, void* out, int64_t M, int64_t N, int
   EpiParams p{};
   p.out = (bf16*)out;
   p.ldo = N;
+  p.err = device_error_ptr();
+  return gemm_dispatch<EPI_STORE>(x, w, M, N, K, p, stream);
+}
+
+int aacc_gemm_bias(const void* x, const void* w, const void* bias, void* out, int64_t M, int64_t N, int64_t K,
+                   cudaStream_t stream) {
+  int st = gemm_check(x, w, M, N, K, "gemm_bias");
+  if (st || M == 0) return st;
+  if (!aligned16(out) || (N % 8)) return set_error(AACC_ERR_INVALID, "gemm_bias: output must be 16-byte aligned rows");
+  EpiParams p{};
+  p.out = (bf16*)out;
+  p.ldo = N;
+  p.bias = (const bf16*)bias;
   p.err = device_error_ptr();
   return gemm_dispatch<EPI_STORE>(x, w, M, N, K, p, stream);
 }

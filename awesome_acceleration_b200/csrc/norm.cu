@@ -13,6 +13,25 @@
 
 namespace aacc {
 
+// x[r][c] <- bf16(x[r][c] + bias[c]), 8 columns per thread (the eager bf16
+// `output + self.bias` after the RowParallel all-reduce).
+__global__ void bias_add_kernel(bf16* __restrict__ x, const bf16* __restrict__ bias, int64_t n8, int64_t cols8) {
+  griddep_wait();
+  griddep_launch();
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  uint4 xv = reinterpret_cast<uint4*>(x)[i];
+  const uint4 bv = reinterpret_cast<const uint4*>(bias)[i % cols8];
+  uint32_t* xs = reinterpret_cast<uint32_t*>(&xv);
+  const uint32_t* bs = reinterpret_cast<const uint32_t*>(&bv);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 a = unpack_bf16(xs[j]), b = unpack_bf16(bs[j]);
+    xs[j] = pack_bf16(a.x + b.x, a.y + b.y);
+  }
+  reinterpret_cast<uint4*>(x)[i] = xv;
+}
+
 template <int V>
 __global__ void __launch_bounds__(kNormMaxThreads) rmsnorm_kernel(const bf16* __restrict__ x,
                                                                   const bf16* __restrict__ w, bf16* __restrict__ y,
@@ -178,6 +197,15 @@ int aacc_splitk_reduce(const float* partial, int splits, void* out, int64_t rows
   const int64_t n8 = rows * cols / 8;
   return check_launch("splitk_reduce", launch_k(splitk_reduce_kernel, dim3((unsigned)((n8 + 255) / 256)), dim3(256),
                                                 0, stream, partial, splits, n8, rows * cols, (bf16*)out));
+}
+
+int aacc_bias_add(void* x, const void* bias, int64_t rows, int64_t cols, cudaStream_t stream) {
+  if (rows < 0 || cols <= 0 || cols % 8 || !aligned16(x) || !aligned16(bias))
+    return set_error(AACC_ERR_INVALID, "bias_add: cols must be a multiple of 8, pointers 16-byte aligned");
+  if (rows == 0) return AACC_OK;
+  const int64_t n8 = rows * cols / 8;
+  return check_launch("bias_add", launch_k(bias_add_kernel, dim3((unsigned)((n8 + 255) / 256)), dim3(256), 0, stream,
+                                           (bf16*)x, (const bf16*)bias, n8, cols / 8));
 }
 
 int aacc_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, void* residual, const void* w, void* y,

@@ -128,13 +128,31 @@ def embed_rmsnorm(ids, table, w, eps: float, residual_out, out):
 
 
 # ---------------------------------------------------------------- GEMMs
-def gemm(x, w, out=None):
+def gemm(x, w, out=None, bias=None):
+    """x [M, K] @ w[N, K]^T (+ bias [N], added in fp32 before the bf16 rounding)."""
     M, K = x.shape
     N = w.shape[0]
     if out is None:
         out = torch.empty((M, N), dtype=BF16, device=x.device)
-    _lib.check(_lib_().aacc_gemm(_p(x), _p(w), _p(out), M, N, K, _stream()), "gemm")
+    if bias is None:
+        _lib.check(_lib_().aacc_gemm(_p(x), _p(w), _p(out), M, N, K, _stream()), "gemm")
+    else:
+        _req(bias, BF16, "bias")
+        if bias.numel() != N:
+            raise ValueError(f"gemm: bias has {bias.numel()} elements, expected {N}")
+        _lib.check(_lib_().aacc_gemm_bias(_p(x), _p(w), _p(bias), _p(out), M, N, K, _stream()), "gemm_bias")
     return out
+
+
+def bias_add(x, bias):
+    """x [..., N] <- bf16(x + bias [N]) in place."""
+    _req(x, BF16, "x")
+    _req(bias, BF16, "bias")
+    N = x.shape[-1]
+    if bias.numel() != N:
+        raise ValueError(f"bias_add: bias has {bias.numel()} elements, expected {N}")
+    _lib.check(_lib_().aacc_bias_add(_p(x), _p(bias), x.numel() // N, N, _stream()), "bias_add")
+    return x
 
 
 def pick_splits(M: int, N: int, K: int, sms: int = 148, cap: int = 16, max_elems: int | None = None) -> int:

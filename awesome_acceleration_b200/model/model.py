@@ -314,10 +314,11 @@ class Qwen3ForCausalLM(nn.Module):
     def export_request_kv(self, slot_idx: int, length: int, device="cpu") -> dict:
         """Per-layer K/V of the first `length` tokens as tensors [length, Hkv, 128]
         (model/model.py:156-166, :386-390).  On the CPU by default, as in the
-        reference; `device` may name another GPU instead, so that a prefill
-        engine hands a request to a decode engine in the same process over
-        NVLink (device-to-device copies of the gathered blocks) rather than
-        through host memory.  import_request_kv takes either."""
+        reference; `device` may name a GPU instead, so that a prefill engine
+        hands a request to a decode engine in the same process with
+        device-to-device copies of the gathered blocks (over NVLink when the
+        target is another GPU) rather than through host memory.
+        import_request_kv takes either."""
         out = []
         for i in range(self.config.num_hidden_layers):
             k, v = self.kv.gather(i, int(slot_idx), int(length))
@@ -333,10 +334,14 @@ class Qwen3ForCausalLM(nn.Module):
         row = int(slot_idx)
         self.kv.reserve(row, int(length))
         self.kv.sync()
-        slots = torch.from_numpy(self.kv.slot_mapping(row, 0, int(length))).to(self.kv.k.device)
-        for i, lp in enumerate(layers):
-            k = lp["k"][:length].to(self.kv.k.device, torch.bfloat16).contiguous()
-            v = lp["v"][:length].to(self.kv.k.device, torch.bfloat16).contiguous()
-            K.kv_store(k.view(length, -1), v.view(length, -1), slots, self.kv.k[i], self.kv.v[i])
+        dev = self.kv.k.device
+        # The store kernel runs on the current device and stream: make that the
+        # cache's device, whichever GPU the caller (or the payload) is on.
+        with torch.cuda.device(dev):
+            slots = torch.from_numpy(self.kv.slot_mapping(row, 0, int(length))).to(dev)
+            for i, lp in enumerate(layers):
+                k = lp["k"][:length].to(dev, torch.bfloat16).contiguous()
+                v = lp["v"][:length].to(dev, torch.bfloat16).contiguous()
+                K.kv_store(k.view(length, -1), v.view(length, -1), slots, self.kv.k[i], self.kv.v[i])
         seqlen = int(layers[0]["seqlen"])
         self.kv.set_lengths([row], [seqlen])

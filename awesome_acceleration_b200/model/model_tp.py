@@ -203,7 +203,11 @@ class Qwen3ForCausalLMTP(nn.Module):
     # ------------------------------------------------------------------ weights
     @classmethod
     def from_state_dict(cls, state_dict: dict, config: Qwen3Config, device, dtype=torch.bfloat16):
-        """Build this rank's model from a full (CPU) state dict."""
+        """Build this rank's model from a full (CPU) state dict.  A tensor
+        already on `device` in `dtype` is used by reference: the model then
+        shares it with the caller's dict, so the full untied lm_head, which
+        fuse_qkv() releases after cutting this rank's shard, is only freed
+        once the caller drops the state dict too."""
         with torch.device("meta"):
             model = cls(config)
         model = model.to_empty(device="cpu").to(dtype)

@@ -6,9 +6,11 @@ constructor arguments, per-rank weight shapes, ``from_linear`` /
 the reference's; the forward bodies run the B200 GEMM (``aacc_gemm``) and the
 NCCL collectives of ``model.distributed``.
 
-Qwen3 has no linear biases; a layer built with ``bias=True`` keeps the
-parameter (so checkpoints load) but its forward raises, because the B200
-GEMM epilogue has no bias term.
+Biases follow the reference: column- and QKV-parallel layers add theirs in
+the GEMM (``F.linear(x, weight, bias)``: fused into the B200 GEMM epilogue,
+fp32 add before the bf16 rounding), a row-parallel layer adds its bias after
+the all-reduce, on TP rank 0 only, the only rank that holds one
+(model/parallel_layers.py:163-170, :197-199).
 """
 from __future__ import annotations
 
@@ -22,15 +24,13 @@ from .distributed import (get_tp_rank, get_tp_world_size, is_distributed, split_
                           tensor_model_parallel_all_gather, tensor_model_parallel_all_reduce)
 
 
-def _gemm_nd(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+def _gemm_nd(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
     lead = x.shape[:-1]
-    out = K.gemm(x.reshape(-1, x.shape[-1]).contiguous(), w)
+    if bias is None:
+        out = K.gemm(x.reshape(-1, x.shape[-1]).contiguous(), w)
+    else:
+        out = K.gemm(x.reshape(-1, x.shape[-1]).contiguous(), w, bias=bias)
     return out.view(*lead, w.shape[0])
-
-
-def _no_bias(layer):
-    if layer.bias is not None:
-        raise NotImplementedError(f"{type(layer).__name__}: bias is not supported on the B200 path")
 
 
 class ColumnParallelLinear(nn.Module):
@@ -53,8 +53,7 @@ class ColumnParallelLinear(nn.Module):
             self.register_parameter("bias", None)
 
     def forward(self, input_: torch.Tensor) -> torch.Tensor:
-        _no_bias(self)
-        out = _gemm_nd(input_, self.weight)
+        out = _gemm_nd(input_, self.weight, self.bias)
         if self.gather_output and is_distributed():
             out = tensor_model_parallel_all_gather(out, dim=-1)
         return out
@@ -88,12 +87,13 @@ class RowParallelLinear(nn.Module):
             self.register_parameter("bias", None)
 
     def forward(self, input_: torch.Tensor) -> torch.Tensor:
-        _no_bias(self)
         if not self.input_is_parallel and is_distributed():
             input_ = split_tensor_along_dim(input_, self.tp_size, dim=-1)
         out = _gemm_nd(input_, self.weight)
         if is_distributed():
             out = tensor_model_parallel_all_reduce(out)
+        if self.bias is not None:  # rank 0 only, after the all-reduce (model/parallel_layers.py:197-199)
+            out = K.bias_add(out.contiguous(), self.bias)
         return out
 
     @classmethod
@@ -147,8 +147,7 @@ class QKVParallelLinear(nn.Module):
     def forward(self, hidden_states: torch.Tensor):
         if hidden_states.dim() not in (2, 3):
             raise ValueError(f"hidden_states must be 2D or 3D, got shape={tuple(hidden_states.shape)}")
-        _no_bias(self)
-        qkv = _gemm_nd(hidden_states, self.weight)
+        qkv = _gemm_nd(hidden_states, self.weight, self.bias)
         qs, ks = self.q_size_per_partition, self.kv_size_per_partition
         lead = hidden_states.shape[:-1]
         q = qkv[..., :qs].reshape(*lead, self.num_q_heads_per_partition, self.head_dim)

@@ -2,13 +2,13 @@
 """Benchmark: Qwen3 greedy generation throughput (output tok/s) on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
-                    [--workload cfg2|attn] [--small]
+                    [--workload cfg2|cfg4|cfg5|attn|gemm] [--small]
 
-Default workload: Qwen3-0.6B architecture, random-init
-bf16 weights, 256 sequences x 1024 uniform-random prompt tokens, 1024 greedy
-output tokens each (EOS ignored), continuous batching, paged KV block 256.
-One "step" is one whole generation job: the packed prefill of all 256
-prompts plus 1023 decode steps (256 x 1024 output tokens).
+Default workload (cfg2): Qwen3-0.6B architecture, random-init bf16 weights,
+256 sequences x 1024 uniform-random prompt tokens, 1024 greedy output tokens
+each (EOS ignored), continuous batching, paged KV block 256.  One "step" is
+one whole generation job: the packed prefill of all 256 prompts plus 1023
+decode steps (256 x 1024 output tokens).
 
 * ``value``: device-timed throughput with the prompts already in HBM and the
   decode loop replaying the captured decode-step graph (next tokens stay on
@@ -21,13 +21,15 @@ prompts plus 1023 decode steps (256 x 1024 output tokens).
   every context token + q in + o out + block-table reads).
 * ``cpu_baseline``: the CPU oracle (a restatement of the reference's own
   PyTorch code path, bf16 on all host cores) over a bounded sample of the
-  same workload.
+  same workload, prefill and decode timed apart.
+* ``tp``: cfg4 (Qwen3-8B, 128 x 2048 in / 512 out) at tensor parallel =
+  the whole world, so the 1/2/4/8-GPU runs record the 8B model's TP scaling.
 
-Under torchrun (N>1) every rank runs an independent replica (DP, weak
+Under torchrun (N>1) every rank runs an independent cfg2 replica (DP, weak
 scaling); ``value`` is the total over ranks divided by the slowest rank.
 ``--impl reference`` times the reference's CPU implementation (the oracle)
 on rank 0 only.  ``--workload attn`` is the decode-attention microbenchmark
-(BASELINE config 3).
+(B = 256, 16 / 8 heads, contexts U[512, 4096], a 65,536-block pool).
 """
 from __future__ import annotations
 
@@ -280,7 +282,7 @@ def phase_summary(cfg2, steps, elapsed, prefill_s, cfg):
     decode_s = (elapsed - prefill_s) / steps
     n_dec = cfg2.out - 1
     kv_tok = 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * cfg.head_dim * 2
-    w_bytes = 1.192e9
+    w_bytes = weight_bytes(cfg)
     ctx = cfg2.prompt + 1 + np.arange(n_dec)  # tokens attended at each decode step
     dec_bytes = n_dec * w_bytes + cfg2.n_seqs * kv_tok * float(ctx.sum() + n_dec)
     ideal = dec_bytes / (pk["hbm_gbs"] * 1e9)
@@ -326,7 +328,7 @@ def attention_roofline(llm, rows, reps=20):
             "state": f"B={B}, ctx={min(ctx)}..{max(ctx)}"}
 
 
-# --------------------------------------------------------------------------- attn microbench (config 3)
+# --------------------------------------------------------------------------- decode-attention microbenchmark
 def run_attn(args, device):
     from awesome_acceleration_b200 import _lib, kernels as Kk
     g = torch.Generator().manual_seed(7)
@@ -391,32 +393,78 @@ def run_attn(args, device):
 
 
 # --------------------------------------------------------------------------- cfg4: Qwen3-8B tensor parallel
-def run_cfg4(args, device):
-    """Qwen3-8B architecture (random-init bf16), 128 seqs x
-    2048 prompt tokens, 512 greedy outputs, tensor parallel over the torchrun
-    world (TP = --tp, DP = world / TP replicas).  Every rank of a TP group runs
-    the same device job; each decode step is one CUDA graph holding the
-    RowParallel all-reduces and the vocab-parallel argmax all-gather."""
+QWEN3_8B_KW = dict(hidden_size=4096, intermediate_size=12288, num_hidden_layers=36, num_attention_heads=32,
+                   num_key_value_heads=8, tie_word_embeddings=False)
+
+
+def weight_bytes(cfg, tp: int = 1) -> float:
+    """bf16 bytes of the weights one decode step streams on each rank: every
+    layer's QKV, o, gate/up and down projections (sharded over tp) plus the
+    lm_head (vocab-sharded over tp; the tied embedding for Qwen3-0.6B)."""
+    H, I, D = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
+    q, kv = cfg.num_attention_heads * D, cfg.num_key_value_heads * D
+    layer = H * (q + 2 * kv) + q * H + 2 * I * H + I * H
+    return 2.0 * (cfg.num_hidden_layers * layer + cfg.vocab_size * H) / tp
+
+
+def exchange_us(rt, rows: int, calls: int = 32, reps: int = 5):
+    """Device time of one RowParallel exchange call (all-reduce + residual add
+    + RMSNorm over NVLink peer memory) on `rows` x hidden bf16 rows: `calls`
+    back-to-back calls captured in one CUDA graph, replayed `reps` times by
+    every rank of the TP group together.  None without the exchange."""
+    ex = rt.comm.exchange
+    if ex is None or rows > ex.max_rows:
+        return None
+    dev = rt.device
+    src = torch.zeros((rows, rt.H), dtype=torch.bfloat16, device=dev)
+    res = torch.zeros_like(src)
+    out = torch.empty_like(src)
+    w = torch.ones(rt.H, dtype=torch.bfloat16, device=dev)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(calls):
+                rt.comm.allreduce_add_rmsnorm(src, 0, res, w, rt.eps, out)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.distributed.barrier(group=rt.comm.cpu_group)
+    g.replay()  # warm
+    torch.cuda.synchronize()
+    torch.distributed.barrier(group=rt.comm.cpu_group)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    e1.synchronize()
+    del g
+    return e0.elapsed_time(e1) * 1e3 / (reps * calls)
+
+
+def run_cfg4(args, device, steps=None, warmup=None, tp=None):
+    """cfg4: Qwen3-8B architecture (random-init bf16), 128 seqs x 2048 prompt
+    tokens, 512 greedy outputs, tensor parallel over the torchrun world (TP =
+    `tp`, default --tp or the world; DP = world / TP replicas).  Every rank of
+    a TP group runs the same device job; each decode step is one CUDA graph
+    holding the RowParallel exchanges and the vocab-parallel argmax
+    all-gather.  `steps` / `warmup` override --steps / --warmup."""
     from awesome_acceleration_b200 import _lib
     from awesome_acceleration_b200.llm_tp import LLMTP
     from awesome_acceleration_b200.model.model import Qwen3Config
-    tp = args.tp or args.world
-    cfg = Qwen3Config(hidden_size=4096, intermediate_size=12288, num_hidden_layers=36, num_attention_heads=32,
-                      num_key_value_heads=8, tie_word_embeddings=False)
+    tp = tp or args.tp or args.world
+    steps = args.steps if steps is None else steps
+    warmup = args.warmup if warmup is None else warmup
+    cfg = Qwen3Config(**QWEN3_8B_KW)
     n_seqs, prompt, out = (16, 512, 32) if args.small else (128, 2048, 512)
     llm = LLMTP(None, max_num_seqs=n_seqs, max_seq_len=prompt + out + 16, enable_tp=args.world > 1, tp_size=tp,
                 config=cfg, seed=7)
     dp = llm.dp_size
     prompts = make_prompts(n_seqs, prompt, cfg.vocab_size, 4321 + llm.dp_rank)
-
-    class C:
-        pass
-    c = C()
-    c.n_seqs, c.prompt, c.out = n_seqs, prompt, out
     lib = _lib.load()
     rt = llm.model._rt()
     stream = torch.cuda.current_stream()
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         rows = device_job(llm, prompts, out)
         torch.cuda.synchronize()
         reset_job(llm, rows)
@@ -427,7 +475,7 @@ def run_cfg4(args, device):
     e0, e1, em = (torch.cuda.Event(enable_timing=True) for _ in range(3))
     elapsed = prefill_s = 0.0
     with ClockSampler(torch.cuda.current_device()) as clk:
-        for _ in range(args.steps):
+        for _ in range(steps):
             e0.record(stream)
             rows = device_job(llm, prompts, out, mark=em)
             e1.record(stream)
@@ -438,39 +486,59 @@ def run_cfg4(args, device):
     _lib.raise_on_device_error("timed region")
     launches = lib.aacc_launch_count() - n0 + (rt.graph_replays - r0) * rt.graph_launches.get(n_seqs, 0)
     t_max = max_over_ranks(args, elapsed)
-    value = dp * n_seqs * out * args.steps / t_max
+    pf_max = max_over_ranks(args, prefill_s)
+    value = dp * n_seqs * out * steps / t_max
     ex = rt.comm.exchange
     exchange = "none" if tp == 1 else "nccl" if ex is None else ("nvlink two-shot" if ex.two_shot else "nvlink one-shot")
+    ex_us = exchange_us(rt, n_seqs) if tp > 1 else None
     pk, kind = peaks()
     n_dec = out - 1
-    kv_tok = 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * 128 * 2 // tp
-    w_bytes = (36 * (4096 * 6144 + 4096 * 4096 + 3 * 4096 * 12288) + cfg.vocab_size * 4096) * 2 / tp
+    kv_tok = 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * cfg.head_dim * 2 // tp
     ctx = prompt + 1 + np.arange(n_dec)
-    dec_bytes = n_dec * w_bytes + n_seqs * kv_tok * float(ctx.sum() + n_dec)
-    decode_s = (elapsed - prefill_s) / args.steps
+    dec_bytes = n_dec * weight_bytes(cfg, tp) + n_seqs * kv_tok * float(ctx.sum() + n_dec)
+    decode_s = (t_max - pf_max) / steps
     llm_stop = getattr(llm, "stop", None)
     if llm_stop:
         llm_stop()
+    rt.comm.close()
     return {
         "metric": f"output tok/s (Qwen3-8B, {n_seqs}x{prompt} in / {out} out, greedy, TP{tp} x DP{dp})",
-        "value": round(value, 1), "unit": "output tok/s", "n_gpus": args.world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(t_max / args.steps * 1e3, 2), "higher_is_better": True,
+        "value": round(value, 1), "unit": "output tok/s", "n_gpus": args.world, "steps": steps,
+        "warmup": warmup, "ms_per_step": round(t_max / steps * 1e3, 2), "higher_is_better": True,
         "scaling": "strong" if dp == 1 else "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (uniform random token ids, random-init weights)",
         "config": {"workload": "cfg4: Qwen3-8B TP" + (" [SMALL]" if args.small else ""), "global_batch": n_seqs * dp,
                    "seq_len": prompt + out, "parallelism": f"tp{tp}" + (f"xdp{dp}" if dp > 1 else ""),
                    "l2": "inputs larger than L2", "row_parallel_exchange": exchange},
         "gpu_launches": int(launches), "clocks": clk.summary(),
-        "phases": {"prefill_ms": round(prefill_s / args.steps * 1e3, 1), "decode_ms": round(decode_s * 1e3, 1),
+        "phases": {"prefill_ms": round(pf_max / steps * 1e3, 1), "decode_ms": round(decode_s * 1e3, 1),
                    "decode_ms_per_step": round(decode_s / n_dec * 1e3, 3),
                    "decode_roofline_frac_per_gpu": round(dec_bytes / (pk["hbm_gbs"] * 1e9) / decode_s, 3),
+                   "exchange_us_per_call": None if ex_us is None else round(ex_us, 2),
                    "peak_kind": kind},
     }
 
 
+def tp_block(args, device):
+    """cfg4 (Qwen3-8B, 128 x 2048 in / 512 out) at TP = the whole world: one
+    warm-up job and two timed jobs, added to the default bench line so that
+    the 1/2/4/8-GPU runs record the tensor-parallel scaling of the 8B model
+    (the north star's TP target) next to the cfg2 DP replicas."""
+    line = run_cfg4(args, device, steps=2, warmup=1, tp=args.world)
+    ph = line["phases"]
+    return {"workload": "cfg4: Qwen3-8B 128 seqs x 2048 prompt / 512 output, greedy, ignore_eos, paged KV block 256",
+            "tp": args.world, "value": line["value"], "unit": "output tok/s", "steps": line["steps"],
+            "warmup": line["warmup"], "ms_per_step": line["ms_per_step"], "prefill_ms": ph["prefill_ms"],
+            "decode_ms_per_step": ph["decode_ms_per_step"],
+            "decode_roofline_frac_per_gpu": ph["decode_roofline_frac_per_gpu"],
+            "row_parallel_exchange": line["config"]["row_parallel_exchange"],
+            "exchange_us_per_call": ph["exchange_us_per_call"], "gpu_launches": line["gpu_launches"],
+            "clocks": line["clocks"], "timing": "CUDA events per job, max over ranks"}
+
+
 # --------------------------------------------------------------------------- cfg5: Qwen3-32B DP x TP
 def run_cfg5(args, device):
-    """Qwen3-32B architecture (random-init bf16), 512
+    """cfg5: Qwen3-32B architecture (random-init bf16), 512
     requests with prompts ~U[256,4096] and outputs ~U[128,1024] (one request
     per sequence with its own max_tokens), greedy, ignore_eos, through the
     engine's public API: the TP-group leader runs continuous batching, the
@@ -604,39 +672,66 @@ def run_gemm(args, device):
 
 
 # --------------------------------------------------------------------------- CPU baseline (oracle)
-def cpu_sample(n_seqs=4, prompt=1024, out=8, seed=99):
+_CPU_ORACLE: dict = {}
+
+
+def cpu_sample(n_seqs=4, prompt=1024, steps=12, seed=99):
     """The reference's CPU code path (restated by the oracle, bf16, all host
-    cores) on a bounded sample of the cfg2 workload: n_seqs prompts of the
-    same length, prefill + (out - 1) decode steps.  Returns (tok/s, info)."""
-    from oracle.qwen3_oracle import Qwen3Oracle, run_greedy
+    cores) on a bounded sample of the cfg2 workload: a packed prefill of
+    n_seqs prompts of `prompt` tokens, then `steps` greedy decode steps of the
+    n_seqs sequences at contexts prompt+1 .. prompt+steps.  The two phases are
+    timed apart.  Returns (decode output tok/s, info with both rates)."""
+    from oracle.qwen3_oracle import Qwen3Oracle, greedy
     from oracle.weights import QWEN3_0_6B, init_weights
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    sd = init_weights(QWEN3_0_6B, seed)
-    orc = Qwen3Oracle(QWEN3_0_6B, sd, torch.bfloat16, num_slots=n_seqs, max_seq_len=prompt + out + 8)
+    key = (n_seqs, prompt, steps, seed)
+    if _CPU_ORACLE.get("key") != key:  # weights and caches built once per process
+        sd = init_weights(QWEN3_0_6B, seed)
+        _CPU_ORACLE.update(key=key, orc=Qwen3Oracle(QWEN3_0_6B, sd, torch.bfloat16, num_slots=n_seqs,
+                                                    max_seq_len=prompt + steps + 8))
+    orc = _CPU_ORACLE["orc"]
     prompts = make_prompts(n_seqs, prompt, QWEN3_0_6B.vocab_size, seed)
-    t0 = time.perf_counter()
-    run_greedy(orc, prompts, out - 1)
-    dt = time.perf_counter() - t0
-    return n_seqs * out / dt, {"cores": cores,
-                                "sample": f"{n_seqs} seqs x {prompt} prompt tokens, prefill + {out - 1} decode "
-                                          f"steps ({n_seqs * out} output tokens, {dt:.1f} s), bf16"}
+    slots = list(range(n_seqs))
+    for s_ in slots:
+        orc.clear_slot(s_)
+    with torch.inference_mode():
+        t0 = time.perf_counter()
+        toks = greedy(orc.prefill(prompts, slots))
+        t1 = time.perf_counter()
+        for s in range(steps):
+            toks = greedy(orc.decode(toks, [prompt + s] * n_seqs, slots))
+        t2 = time.perf_counter()
+    pre, dec = n_seqs * prompt / (t1 - t0), n_seqs * steps / (t2 - t1)
+    return dec, {"cores": cores, "prefill_tok_per_s": round(pre, 1), "decode_tok_per_s": round(dec, 3),
+                 "sample": f"{n_seqs} seqs x {prompt} prompt tokens: packed prefill ({t1 - t0:.1f} s, "
+                           f"{pre:.0f} prompt tok/s) then {steps} greedy decode steps at contexts "
+                           f"{prompt + 1}..{prompt + steps} ({t2 - t1:.1f} s); value = decode output tok/s "
+                           f"(the phase that produces 1023 of every 1024 output tokens), bf16"}
+
+
+def cpu_baseline_entry(v, info):
+    return {"value": round(v, 3), "unit": "output tok/s", "cores": info["cores"], "kind": "port",
+            "phase": "decode", "prefill_tok_per_s": info["prefill_tok_per_s"],
+            "decode_tok_per_s": info["decode_tok_per_s"], "sample": info["sample"]}
 
 
 def run_reference(args):
-    vals = []
+    vals, infos = [], []
     for i in range(args.warmup + args.steps):
         v, info = cpu_sample()
         if i >= args.warmup:
             vals.append(v)
+            infos.append(info)
     v = statistics.mean(vals)
+    info = dict(infos[-1], prefill_tok_per_s=round(statistics.mean(x["prefill_tok_per_s"] for x in infos), 1),
+                decode_tok_per_s=round(v, 3))
     return {"impl": "reference", "metric": "output tok/s (Qwen3-0.6B, 256x1024 in / 1024 out, greedy)",
             "value": round(v, 3), "unit": "output tok/s", "n_gpus": args.world, "steps": args.steps,
             "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "cfg2 (bounded CPU sample)", "parallelism": "cpu"},
-            "cpu_baseline": {"value": round(v, 3), "unit": "output tok/s", "cores": info["cores"], "kind": "port",
-                             "sample": info["sample"]},
+            "config": {"workload": "cfg2 (bounded CPU sample: decode phase at context ~1024)", "parallelism": "cpu"},
+            "cpu_baseline": cpu_baseline_entry(v, info),
             "e2e": {"value": round(v, 3), "unit": "output tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -664,6 +759,8 @@ def main():
     ap.add_argument("--tp", type=int, default=0, help="cfg4/cfg5: tensor-parallel size (default: the whole world)")
     ap.add_argument("--small", action="store_true", help="small case for profiler captures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tp-block", action="store_true",
+                    help="cfg2: skip the cfg4 (Qwen3-8B) tensor-parallel block at TP = the world")
     ap.add_argument("--decode", action="store_true", help="gemm workload: decode-batch shapes")
     ap.add_argument("--midrun", action="store_true",
                     help="cfg2 profiler case: 1536-token prompts (the job's mean decode context), 7 decode steps")
@@ -686,10 +783,14 @@ def main():
     try:
         line = {"attn": run_attn, "gemm": run_gemm, "cfg2": run_cfg2, "cfg4": run_cfg4,
                 "cfg5": run_cfg5}[args.workload](args, device)
+        if args.workload == "cfg2" and not (args.small or args.profile or args.no_tp_block):
+            import gc
+            gc.collect()
+            torch.cuda.empty_cache()
+            line["tp"] = tp_block(args, device)
         if args.world == 1 and args.workload == "cfg2" and not (args.no_cpu_baseline or args.profile):
             v, info = cpu_sample()
-            line["cpu_baseline"] = {"value": round(v, 3), "unit": "output tok/s", "cores": info["cores"],
-                                    "kind": "port", "sample": info["sample"]}
+            line["cpu_baseline"] = cpu_baseline_entry(v, info)
         if args.rank == 0:
             print(json.dumps(line), flush=True)
     finally:

@@ -185,6 +185,17 @@ int aacc_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, voi
 int aacc_gemm(const void* x, const void* w, void* out, int64_t M, int64_t N, int64_t K,
               cudaStream_t stream);
 
+/* out[M][N] = bf16(x[M][K] @ w[N][K]^T + bias[N]): the bias added in fp32
+ * before the rounding, as a fused-bias F.linear does.  Column-parallel and
+ * QKV-parallel layers built with bias=True (model/parallel_layers.py:72-89,
+ * :299-342: F.linear(x, weight, bias)). */
+int aacc_gemm_bias(const void* x, const void* w, const void* bias, void* out, int64_t M, int64_t N, int64_t K,
+                   cudaStream_t stream);
+
+/* x[rows][cols] <- bf16(x + bias[cols]): the RowParallel bias, added after
+ * the all-reduce on TP rank 0 only (model/parallel_layers.py:197-199). */
+int aacc_bias_add(void* x, const void* bias, int64_t rows, int64_t cols, cudaStream_t stream);
+
 /* Split-K GEMM: partial[s][M][N] (fp32) = x[:, Ks] @ w[:, Ks]^T for the s-th
  * of `splits` equal K ranges (splits must divide K/64).  Spreads a small
  * decode GEMM (N = hidden, e.g. o_proj / down_proj) over every SM; the

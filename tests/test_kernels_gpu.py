@@ -383,6 +383,24 @@ def test_lm_head_argmax(cuda, M, V):
     assert torch.equal(t2.cpu(), tokens.cpu())
 
 
+@pytest.mark.parametrize("M,N,Kd", [(1, 1024, 1024), (77, 384, 256), (300, 3072, 1024)])
+def test_gemm_bias_and_bias_add(cuda, M, N, Kd):
+    """Fused-bias GEMM (fp32 add before the rounding, F.linear(x, w, b)) and the
+    RowParallel post-all-reduce bias add (bf16(out + b))."""
+    g = torch.Generator().manual_seed(M + N)
+    x = torch.randn((M, Kd), generator=g).to(BF)
+    w = (torch.randn((N, Kd), generator=g) * 0.05).to(BF)
+    b = torch.randn(N, generator=g).to(BF)
+    out = K().gemm(x.to(cuda), w.to(cuda), bias=b.to(cuda))
+    ref = (x.float() @ w.float().t() + b.float())
+    err = (out.cpu().float() - ref).abs().max().item()
+    assert err <= 1e-2 * ref.abs().max().item() + 1e-3, err
+    y = torch.randn((M, N), generator=g).to(BF)
+    yd = y.to(cuda)
+    K().bias_add(yd, b.to(cuda))
+    assert torch.equal(yd.cpu(), (y.float() + b.float()).to(BF))
+
+
 def test_argmax_merge_ties_lowest_index(cuda):
     val = torch.tensor([[1.0, 5.0], [3.0, 5.0], [3.0, 2.0]], device=cuda)      # [shards=3, M=2]
     idx = torch.tensor([[10, 7], [20, 3], [5, 1]], dtype=torch.int64, device=cuda)

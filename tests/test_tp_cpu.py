@@ -81,7 +81,10 @@ def _layers(rank, world):
     from awesome_acceleration_b200.model import distributed as D
     from awesome_acceleration_b200.model import parallel_layers as PL
     D.init_distributed(world, backend="gloo", timeout_s=30)
-    kernels.gemm = lambda x, w, out=None: (x.float() @ w.float().t()).to(x.dtype)  # CPU stand-in (test only)
+    # CPU stand-ins for the GEMM and the bias add (test only)
+    kernels.gemm = lambda x, w, out=None, bias=None: (x.float() @ w.float().t()
+                                                      + (0 if bias is None else bias.float())).to(x.dtype)
+    kernels.bias_add = lambda x, b: x.add_(b)
     g = torch.Generator().manual_seed(0)
     H, I, Hq, Hkv, Dh = 64, 96, 4, 2, 16
     lin = torch.nn.Linear(H, I, bias=False)
@@ -97,7 +100,33 @@ def _layers(rank, world):
     xs = x[..., rank * I // world:(rank + 1) * I // world].contiguous()
     y = row(xs)  # partial matmul + all-reduce over the TP group
     assert torch.allclose(y, x @ down.weight.t(), atol=1e-4)
+    # biases (model/parallel_layers.py:82, :163-170, :197-199): a column shard adds its slice of
+    # the bias in the GEMM; a row-parallel layer keeps its bias on rank 0 only and adds it
+    # after the all-reduce, so only rank 0's output carries it
+    lin_b = torch.nn.Linear(H, I, bias=True)
+    lin_b.weight.data, lin_b.bias.data = torch.randn((I, H), generator=g), torch.randn(I, generator=g)
+    col_b = PL.ColumnParallelLinear.from_linear(lin_b)
+    sl = slice(rank * I // world, (rank + 1) * I // world)
+    assert torch.equal(col_b.bias, lin_b.bias[sl])
+    xh = torch.randn((6, H), generator=g)
+    assert torch.allclose(col_b(xh), xh @ lin_b.weight[sl].t() + lin_b.bias[sl], atol=1e-4)
+    down_b = torch.nn.Linear(I, H, bias=True)
+    down_b.weight.data, down_b.bias.data = torch.randn((H, I), generator=g), torch.randn(H, generator=g)
+    row_b = PL.RowParallelLinear.from_linear(down_b)
+    assert (row_b.bias is not None) == (rank == 0)
+    y = row_b(xs)
+    exp = x @ down_b.weight.t() + (down_b.bias if rank == 0 else 0)
+    assert torch.allclose(y, exp, atol=1e-4)
     full = torch.randn(((Hq + 2 * Hkv) * Dh, H), generator=g)
+    fb = torch.randn((Hq + 2 * Hkv) * Dh, generator=g)
+    qkv_b = PL.QKVParallelLinear.from_fused_qkv(full, fb, H, Hq, Hkv, Dh)
+    qr, kr = Hq // world * Dh, Hkv // world * Dh
+    exp_b = torch.cat([fb[rank * qr:(rank + 1) * qr], fb[Hq * Dh + rank * kr:Hq * Dh + (rank + 1) * kr],
+                       fb[(Hq + Hkv) * Dh + rank * kr:(Hq + Hkv) * Dh + (rank + 1) * kr]])
+    assert torch.equal(qkv_b.bias, exp_b)
+    qb, kb, vb = qkv_b(xh)
+    assert torch.allclose(torch.cat([qb.flatten(1), kb.flatten(1), vb.flatten(1)], 1),
+                          xh @ qkv_b.weight.t() + exp_b, atol=1e-4)
     qkv = PL.QKVParallelLinear.from_fused_qkv(full, None, H, Hq, Hkv, Dh)
     qr, kr = Hq // world * Dh, Hkv // world * Dh
     exp = torch.cat([full[rank * qr:(rank + 1) * qr], full[Hq * Dh + rank * kr:Hq * Dh + (rank + 1) * kr],
