@@ -43,6 +43,12 @@ SIGNATURES: dict[str, tuple] = {
     "aacc_gemm_silu_mul": (I32, [P, P, P, I64, I64, I64, P]),
     "aacc_gemm_splitk": (I32, [P, P, P, I64, I64, I64, I32, P]),
     "aacc_gemm_bias": (I32, [P, P, P, P, I64, I64, I64, P]),
+    "aacc_gemm_cluster": (I32, [P, P, P, I64, I64, I64, I32, P]),
+    "aacc_gemm_silu_mul_cluster": (I32, [P, P, P, I64, I64, I64, I32, P]),
+    "aacc_qkv_norm_rope_store_cluster": (I32, [P, P, P, P, F32, P, P, I64, P, P, P, P, I64, I32, I32, I32, I64, I64,
+                                               I32, P]),
+    "aacc_gemm_cluster_plan": (I32, [I64, I64, I64, P, P, P]),
+    "aacc_gemm_cluster_capacity": (I64, [I32, I32]),
     "aacc_bias_add": (I32, [P, P, I64, I64, P]),
     "aacc_splitk_add_rmsnorm": (I32, [P, I32, P, P, P, I64, I64, F32, P]),
     "aacc_splitk_reduce": (I32, [P, I32, P, I64, I64, P]),

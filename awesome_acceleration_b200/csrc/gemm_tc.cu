@@ -26,6 +26,7 @@
 #include "common.cuh"
 #include "host.h"
 #include "sample.cuh"
+#include "tcgen05.cuh"
 
 namespace aacc {
 
@@ -73,74 +74,6 @@ struct GemmCfg {
   static constexpr int TMEM_COLS = MT * BN;  // 128, 256 or 512
   static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 + 256;
 };
-
-// ---- tcgen05 wrappers ------------------------------------------------------
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
-  // K-major, 128-byte swizzle: 8-row core groups 1024 bytes apart (SBO),
-  // leading offset unused (1), descriptor version 1, layout SWIZZLE_128B (2).
-  return (uint64_t)((saddr & 0x3FFFF) >> 4) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
-         (uint64_t(1) << 46) | (uint64_t(2) << 61);
-}
-template <int BN>
-__device__ __forceinline__ constexpr uint32_t umma_idesc_bf16() {
-  // D fp32 (bit 4), A bf16 (bits 7-9 = 1), B bf16 (bits 10-12 = 1), both
-  // K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28 (M = 128).
-  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(128 >> 4) << 24);
-}
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
-}
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void store16_bf16(bf16* dst, const float (&v)[16]) {
-  uint4 a, b;
-  a.x = pack_bf16(v[0], v[1]);
-  a.y = pack_bf16(v[2], v[3]);
-  a.z = pack_bf16(v[4], v[5]);
-  a.w = pack_bf16(v[6], v[7]);
-  b.x = pack_bf16(v[8], v[9]);
-  b.y = pack_bf16(v[10], v[11]);
-  b.z = pack_bf16(v[12], v[13]);
-  b.w = pack_bf16(v[14], v[15]);
-  reinterpret_cast<uint4*>(dst)[0] = a;
-  reinterpret_cast<uint4*>(dst)[1] = b;
-}
-__device__ __forceinline__ void load16_bf16(const bf16* src, float (&v)[16]) {
-  uint4 a = reinterpret_cast<const uint4*>(src)[0], b = reinterpret_cast<const uint4*>(src)[1];
-  const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
-  const uint32_t* pb = reinterpret_cast<const uint32_t*>(&b);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    float2 f = unpack_bf16(pa[j]);
-    v[2 * j] = f.x;
-    v[2 * j + 1] = f.y;
-    f = unpack_bf16(pb[j]);
-    v[8 + 2 * j] = f.x;
-    v[8 + 2 * j + 1] = f.y;
-  }
-}
 
 // ---- epilogues: one thread = one output row, 128 columns ------------------
 // `tcol` is the TMEM address of column 0 of this 128-column group for this

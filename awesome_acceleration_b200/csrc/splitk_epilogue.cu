@@ -10,78 +10,35 @@
 //                       interleaved in groups of 64.
 #include "common.cuh"
 #include "host.h"
+#include "qkv_epilogue.cuh"
 
 namespace aacc {
 
 __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 
 __global__ void __launch_bounds__(128)
-    splitk_qkv_kernel(const float* __restrict__ part, int S, int64_t M, const bf16* __restrict__ qn_w,
-                      const bf16* __restrict__ kn_w, float eps, const int64_t* __restrict__ positions,
-                      const bf16* __restrict__ rope, int64_t max_pos, const int64_t* __restrict__ slot_mapping,
-                      bf16* __restrict__ q_out, bf16* __restrict__ k_cache, bf16* __restrict__ v_cache,
-                      int64_t num_slots, int Hq, int Hkv, int bs, unsigned* err) {
+    splitk_qkv_kernel(const float* __restrict__ part, int S, int64_t M, QkvEpi a) {
   griddep_wait();
   griddep_launch();
-  const int heads = Hq + 2 * Hkv;
+  const int heads = a.Hq + 2 * a.Hkv;
   const int64_t item = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
   if (item >= M * heads) return;
   const int lane = threadIdx.x & 31;
   const int64_t m = item / heads;
   const int hh = (int)(item % heads);
   const int64_t N = (int64_t)heads * 128;
-  const int c = 4 * lane;  // column within the head
-  const float* src = part + m * N + (int64_t)hh * 128 + c;
-  float4 a = ld4(src);
+  const float* src = part + m * N + (int64_t)hh * 128 + 4 * lane;
+  float4 s4 = ld4(src);
 #pragma unroll 4  // several splits' loads in flight; additions stay in split order
   for (int s = 1; s < S; ++s) {
     const float4 b = ld4(src + (int64_t)s * M * N);
-    a.x += b.x;
-    a.y += b.y;
-    a.z += b.z;
-    a.w += b.w;
+    s4.x += b.x;
+    s4.y += b.y;
+    s4.z += b.z;
+    s4.w += b.w;
   }
-  float x[4] = {rbf(a.x), rbf(a.y), rbf(a.z), rbf(a.w)};
-  const bool is_q = hh < Hq, is_k = !is_q && hh < Hq + Hkv;
-  bf16* dst = nullptr;
-  if (is_q) {
-    dst = q_out + (m * Hq + hh) * 128;
-  } else {
-    const int64_t slot = slot_mapping[m];
-    if (slot >= num_slots && lane == 0) report(err, ERR_SLOT_OOB);
-    if (slot >= 0 && slot < num_slots) {
-      const int kvh = is_k ? hh - Hq : hh - Hq - Hkv;
-      dst = (is_k ? k_cache : v_cache) + (((slot / bs) * Hkv + kvh) * bs + slot % bs) * 128;
-    }
-  }
-  if (is_q || is_k) {
-    float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
-    ss = warp_sum(ss);
-    const float r = rsqrtf(ss / 128.f + eps);
-    const bf16* nw = (is_q ? qn_w : kn_w) + c;
-    float y[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) y[i] = rbf(bf(nw[i]) * rbf(x[i] * r));
-    int64_t pos = positions[m];
-    if (pos < 0 || pos >= max_pos) {
-      if (lane == 0) report(err, ERR_POS_OOB);
-      pos = 0;
-    }
-    const int ci = c & 63;  // frequency index (the table's cos/sin repeat every 64 columns)
-    const bf16* cs = rope + pos * 128;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float partner = __shfl_xor_sync(0xffffffffu, y[i], 16);  // column c+i +/- 64
-      const float cv = bf(cs[ci + i]), sv = bf(cs[64 + ci + i]);
-      x[i] = (c < 64) ? rbf(y[i] * cv) + rbf(-partner * sv) : rbf(y[i] * cv) + rbf(partner * sv);
-    }
-  }
-  if (dst) {
-    uint2 o;
-    o.x = pack_bf16(x[0], x[1]);
-    o.y = pack_bf16(x[2], x[3]);
-    *reinterpret_cast<uint2*>(dst + c) = o;
-  }
+  const float acc[4] = {s4.x, s4.y, s4.z, s4.w};
+  qkv_head_epilogue(acc, lane, m, hh, a);
 }
 
 __global__ void splitk_silu_kernel(const float* __restrict__ part, int S, int64_t M, int64_t I,
@@ -112,10 +69,7 @@ __global__ void splitk_silu_kernel(const float* __restrict__ part, int S, int64_
   }
   float r[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float gg = rbf(g[i]);
-    r[i] = rbf(gg / (1.0f + expf(-gg))) * rbf(u[i]);
-  }
+  for (int i = 0; i < 8; ++i) r[i] = silu_mul(g[i], u[i]);
   uint4 o;
   o.x = pack_bf16(r[0], r[1]);
   o.y = pack_bf16(r[2], r[3]);
@@ -142,12 +96,12 @@ int aacc_splitk_qkv_norm_rope_store(const float* partial, int splits, const void
   if (!aligned16(partial) || !aligned16(q_out) || !aligned16(k_cache) || !aligned16(v_cache))
     return set_error(AACC_ERR_INVALID, "splitk_qkv_norm_rope_store: pointers must be 16-byte aligned");
   const int64_t items = M * (num_q_heads + 2 * num_kv_heads);
-  return check_launch(
-      "splitk_qkv_norm_rope_store",
-      launch_k(splitk_qkv_kernel, dim3((unsigned)((items + 3) / 4)), dim3(128), 0, stream, partial, splits, M,
-               (const bf16*)q_norm_w, (const bf16*)k_norm_w, eps, positions, (const bf16*)rope_cos_sin, max_pos,
-               slot_mapping, (bf16*)q_out, (bf16*)k_cache, (bf16*)v_cache, num_blocks * block_size, num_q_heads,
-               num_kv_heads, block_size, device_error_ptr()));
+  QkvEpi a{(const bf16*)q_norm_w, (const bf16*)k_norm_w, eps, positions, (const bf16*)rope_cos_sin, max_pos,
+           slot_mapping, (bf16*)q_out, (bf16*)k_cache, (bf16*)v_cache, num_blocks * block_size, num_q_heads,
+           num_kv_heads, block_size, device_error_ptr()};
+  return check_launch("splitk_qkv_norm_rope_store",
+                      launch_k(splitk_qkv_kernel, dim3((unsigned)((items + 3) / 4)), dim3(128), 0, stream, partial,
+                               splits, M, a));
 }
 
 int aacc_splitk_silu_mul(const float* partial, int splits, void* out, int64_t M, int64_t I, cudaStream_t stream) {

@@ -233,6 +233,57 @@ def qkv_norm_rope_store(x, w_qkv, q_norm_w, k_norm_w, eps: float, positions, rop
     return q_out
 
 
+# ---------------------------------------------------------------- decode projections (cluster split-K)
+CLUSTER_MAX_ROWS = 256
+
+
+def gemm_cluster(x, w, out=None, splits: int = 0):
+    """bf16 x [M, K] @ w [N, K]^T for a decode batch (M <= 256), K split over a
+    thread-block cluster and summed through distributed shared memory."""
+    M, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=BF16, device=x.device)
+    _lib.check(_lib_().aacc_gemm_cluster(_p(x), _p(w), _p(out), M, N, K, splits, _stream()), "gemm_cluster")
+    return out
+
+
+def gemm_silu_mul_cluster(x, w_gate_up, out=None, splits: int = 0):
+    M, K = x.shape
+    I = w_gate_up.shape[0] // 2
+    if out is None:
+        out = torch.empty((M, I), dtype=BF16, device=x.device)
+    _lib.check(_lib_().aacc_gemm_silu_mul_cluster(_p(x), _p(w_gate_up), _p(out), M, I, K, splits, _stream()),
+               "gemm_silu_mul_cluster")
+    return out
+
+
+def qkv_norm_rope_store_cluster(x, w_qkv, q_norm_w, k_norm_w, eps: float, positions, rope_cos_sin, slot_mapping,
+                                k_cache, v_cache, num_q_heads: int, q_out=None, splits: int = 0):
+    M, K = x.shape
+    nb, hkv, bs, _ = k_cache.shape
+    if q_out is None:
+        q_out = torch.empty((M, num_q_heads, 128), dtype=BF16, device=x.device)
+    _lib.check(_lib_().aacc_qkv_norm_rope_store_cluster(
+        _p(x), _p(w_qkv), _p(q_norm_w), _p(k_norm_w), eps, _p(positions), _p(rope_cos_sin), rope_cos_sin.shape[0],
+        _p(slot_mapping), _p(q_out), _p(k_cache), _p(v_cache), nb, num_q_heads, hkv, bs, M, K, splits, _stream()),
+        "qkv_norm_rope_store_cluster")
+    return q_out
+
+
+def gemm_cluster_plan(M: int, N: int, K: int) -> tuple[int, int, int]:
+    """(tile rows / 128, tiles over M, splits) the cluster GEMMs pick for M x N x K on this GPU."""
+    mt, mtiles, splits = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    _lib.check(_lib_().aacc_gemm_cluster_plan(M, N, K, ctypes.byref(mt), ctypes.byref(mtiles), ctypes.byref(splits)),
+               "gemm_cluster_plan")
+    return mt.value, mtiles.value, splits.value
+
+
+def gemm_cluster_capacity(tile_rows_128: int, splits: int) -> int:
+    """CTAs of the cluster GEMM with clusters of `splits` that fit on this GPU at once."""
+    return int(_lib_().aacc_gemm_cluster_capacity(tile_rows_128, splits))
+
+
 def lm_head_workspace_bytes(M: int, vocab: int) -> int:
     return int(_lib_().aacc_lm_head_workspace_bytes(M, vocab))
 

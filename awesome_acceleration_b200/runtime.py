@@ -219,6 +219,7 @@ class Qwen3Runtime:
         self.max_batch = max_batch
         self.use_graphs = use_graphs
         self.chunk = prefill_chunk_tokens
+        self.cluster_gemm = os.environ.get("AACC_CLUSTER_GEMM", "1") != "0"
         self.device = embed.device
         self.max_context = kv.max_blocks * kv.block_size
         self.buf = _DecodeBuffers(max_batch, hidden, self.Hq, self.I, self.vocab_local, tp, self.max_context,
@@ -247,10 +248,20 @@ class Qwen3Runtime:
             return 1
         return K.pick_splits(M, w.shape[0], w.shape[1], max_elems=part.numel())
 
+    def _cluster(self, M, part) -> bool:
+        """Decode-sized batches run the cluster split-K projections (one launch
+        each, epilogue fused, partials summed in distributed shared memory);
+        AACC_CLUSTER_GEMM=0 selects split-K through HBM + epilogue kernels."""
+        return part is not None and 0 < M <= K.CLUSTER_MAX_ROWS and self.cluster_gemm
+
     def _qkv(self, i, lw, x, positions, slot_map, q, part):
         """Fused QKV projection + q/k-norm + RoPE + KV store (model/model.py:219-226)."""
         kv = self.kv
         M = x.shape[0]
+        if self._cluster(M, part):
+            K.qkv_norm_rope_store_cluster(x, lw.wqkv, lw.q_norm, lw.k_norm, self.eps, positions, self.rope, slot_map,
+                                          kv.k[i], kv.v[i], self.Hq, q_out=q)
+            return
         splits = self._splits(M, lw.wqkv, part)
         if splits > 1:
             N = lw.wqkv.shape[0]
@@ -265,6 +276,9 @@ class Qwen3Runtime:
     def _gate_up(self, lw, x, act, part):
         """gate/up projection + SiLU-mul (model/model.py:189-190)."""
         M = x.shape[0]
+        if self._cluster(M, part):
+            K.gemm_silu_mul_cluster(x, lw.w_gate_up, out=act)
+            return
         splits = self._splits(M, lw.w_gate_up, part)
         if splits > 1:
             N = lw.w_gate_up.shape[0]
@@ -280,11 +294,18 @@ class Qwen3Runtime:
         the fp32 partials inside the norm kernel; under TP the bf16 partial
         output is all-reduced first (RowParallelLinear, parallel_layers.py:190-195)."""
         M = inp.shape[0]
-        splits = self._splits(M, w, part)
         # The NVLink exchange only runs inside captured decode graphs: there the
         # ranks replay in step, while eager launches (prefill, capture warm-up)
         # can lag by a host stall, which NCCL's blocking collectives absorb.
         graph = self.comm.size > 1 and torch.cuda.is_current_stream_capturing()
+        if self._cluster(M, part):
+            K.gemm_cluster(inp, w, out=delta)
+            if graph and self.comm.allreduce_add_rmsnorm(delta, 0, res, norm_w, self.eps, x):
+                return
+            self.comm.all_reduce(delta)
+            K.add_rmsnorm(delta, res, norm_w, self.eps, out=x)
+            return
+        splits = self._splits(M, w, part)
         if splits > 1:
             pv = part[:splits * M * w.shape[0]].view(splits, M, w.shape[0])
             K.gemm_splitk(inp, w, pv, splits)

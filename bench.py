@@ -617,15 +617,145 @@ def run_cfg5(args, device):
 
 
 # --------------------------------------------------------------------------- prefill GEMMs (tensor pipe)
+def run_decode_projections(args, device):
+    """The decode projections of one layer as the engine runs them at B rows
+    (cfg2: Qwen3-0.6B, B = 256): QKV + q/k-norm + RoPE + KV store, o_proj +
+    residual add + RMSNorm, gate/up + SiLU, down + residual add + RMSNorm, over
+    28 layers of distinct weights (840 MB, so every layer streams its weights
+    from HBM), captured in one CUDA graph per variant:
+      * cluster: cluster split-K kernels (partials in distributed shared memory,
+        epilogues fused) + add_rmsnorm;
+      * splitk: split-K partials through HBM + epilogue kernels.
+    Reports us per layer for the whole sequence and for each projection alone."""
+    from awesome_acceleration_b200 import _lib, kernels as Kk
+    from awesome_acceleration_b200.runtime import interleave_gate_up, rope_table
+    B = args.batch or (32 if args.small else 256)
+    L, H, I, hq, hkv, bs = 28, 1024, 3072, 16, 8, 256
+    g = torch.Generator(device=device).manual_seed(3)
+
+    def rnd(*shape, std=0.02):
+        return (torch.randn(shape, generator=g, device=device) * std).to(torch.bfloat16)
+
+    layers = []
+    for _ in range(L):
+        layers.append({"qkv": rnd((hq + 2 * hkv) * 128, H), "o": rnd(H, hq * 128),
+                       "gu": interleave_gate_up(rnd(I, H), rnd(I, H)).contiguous(), "d": rnd(H, I),
+                       "qn": torch.ones(128, dtype=torch.bfloat16, device=device),
+                       "kn": torch.ones(128, dtype=torch.bfloat16, device=device),
+                       "ln": torch.ones(H, dtype=torch.bfloat16, device=device)})
+    x, res = rnd(B, H, std=1.0), rnd(B, H, std=1.0)
+    attn, act, delta = rnd(B, hq * 128, std=1.0), rnd(B, I, std=1.0), rnd(B, H)
+    q = torch.empty((B, hq, 128), dtype=torch.bfloat16, device=device)
+    rope = rope_table(4096, 128, 1e6, device)
+    pos = torch.randint(0, 4096, (B,), device=device)
+    nb = (B + bs - 1) // bs + 1
+    kc = torch.zeros((nb, hkv, bs, 128), dtype=torch.bfloat16, device=device)
+    vc = torch.zeros_like(kc)
+    slots = torch.randperm(nb * bs, device=device)[:B]
+    part = torch.empty(max(8 << 20, 16 * B * H), dtype=torch.float32, device=device)
+
+    def pv(M, N, splits):
+        return part[:splits * M * N].view(splits, M, N)
+
+    def qkv(lw, cluster):
+        if cluster:
+            Kk.qkv_norm_rope_store_cluster(x, lw["qkv"], lw["qn"], lw["kn"], 1e-6, pos, rope, slots, kc, vc, hq,
+                                           q_out=q)
+            return
+        N = lw["qkv"].shape[0]
+        sp = Kk.pick_splits(B, N, H, max_elems=part.numel())
+        if sp > 1:
+            Kk.gemm_splitk(x, lw["qkv"], pv(B, N, sp), sp)
+            Kk.splitk_qkv_norm_rope_store(pv(B, N, sp), sp, lw["qn"], lw["kn"], 1e-6, pos, rope, slots, kc, vc, hq, q)
+        else:
+            Kk.qkv_norm_rope_store(x, lw["qkv"], lw["qn"], lw["kn"], 1e-6, pos, rope, slots, kc, vc, hq, q_out=q)
+
+    def row(inp, wt, ln, cluster):
+        if cluster:
+            Kk.gemm_cluster(inp, wt, out=delta)
+            Kk.add_rmsnorm(delta, res, ln, 1e-6, out=x)
+            return
+        N, Kd = wt.shape
+        sp = Kk.pick_splits(B, N, Kd, max_elems=part.numel())
+        if sp > 1:
+            Kk.gemm_splitk(inp, wt, pv(B, N, sp), sp)
+            Kk.splitk_add_rmsnorm(pv(B, N, sp), sp, res, ln, 1e-6, out=x)
+        else:
+            Kk.gemm(inp, wt, out=delta)
+            Kk.add_rmsnorm(delta, res, ln, 1e-6, out=x)
+
+    def gate_up(lw, cluster):
+        if cluster:
+            Kk.gemm_silu_mul_cluster(x, lw["gu"], out=act)
+            return
+        sp = Kk.pick_splits(B, 2 * I, H, max_elems=part.numel())
+        if sp > 1:
+            Kk.gemm_splitk(x, lw["gu"], pv(B, 2 * I, sp), sp)
+            Kk.splitk_silu_mul(pv(B, 2 * I, sp), sp, act)
+        else:
+            Kk.gemm_silu_mul(x, lw["gu"], out=act)
+
+    ops = {"qkv": lambda lw, c: qkv(lw, c), "o_norm": lambda lw, c: row(attn, lw["o"], lw["ln"], c),
+           "gate_up": lambda lw, c: gate_up(lw, c), "down_norm": lambda lw, c: row(act, lw["d"], lw["ln"], c)}
+    seqs = {"layer": list(ops)} | {k: [k] for k in ops}
+    stream = torch.cuda.current_stream()
+    res_us = {}
+    pk, kind = peaks()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        for variant in ("cluster", "splitk"):
+            cl = variant == "cluster"
+            for name, seq in seqs.items():
+                def body():
+                    for lw in layers:
+                        for op in seq:
+                            ops[op](lw, cl)
+                body()  # eager warm-up (plans, tensor maps, smem attributes)
+                torch.cuda.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                side = torch.cuda.Stream()
+                side.wait_stream(stream)
+                with torch.cuda.stream(side):
+                    with torch.cuda.graph(graph, stream=side):
+                        body()
+                stream.wait_stream(side)
+                for _ in range(args.warmup):
+                    graph.replay()
+                ts = []
+                for _ in range(args.steps):
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    graph.replay()
+                    e1.record(stream)
+                    e1.synchronize()
+                    ts.append(e0.elapsed_time(e1) / 1e3)
+                del graph
+                res_us[f"{variant}.{name}"] = round(statistics.median(ts) / L * 1e6, 2)
+    _lib.raise_on_device_error("decode projections")
+    w_layer = 2 * ((hq + 2 * hkv) * 128 * H + H * hq * 128 + 2 * I * H + H * I)
+    flops = 2 * B * w_layer / 2
+    t = res_us["cluster.layer"] * 1e-6
+    plans = {"qkv": Kk.gemm_cluster_plan(B, (hq + 2 * hkv) * 128, H), "o": Kk.gemm_cluster_plan(B, H, hq * 128),
+             "gate_up": Kk.gemm_cluster_plan(B, 2 * I, H), "down": Kk.gemm_cluster_plan(B, H, I)}
+    return {"metric": f"decode projections us per layer (Qwen3-0.6B shapes, B={B})", "value": res_us["cluster.layer"],
+            "unit": "us per layer", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "decode projections of one layer, 28 layers of distinct weights per graph",
+                       "per_variant_us": res_us, "cluster_plans (mt, m_tiles, splits)": plans,
+                       "l2": "weights 840 MB > L2"},
+            "roofline": {"bound": "hbm", "achieved": round(w_layer / t / 1e9, 1), "peak": pk["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(w_layer / t / 1e9 / pk["hbm_gbs"], 3), "traffic": None,
+                         "peak_kind": kind, "tensor_tflops": round(flops / t / 1e12, 1)},
+            "gpu_launches": None, "clocks": clk.summary()}
+
+
 def run_gemm(args, device):
     """The four cfg2 projections on one prefill chunk (M tokens) or, with
     --decode, on one decode batch (M = 256 rows; weight-bandwidth bound)."""
+    if args.decode:
+        return run_decode_projections(args, device)
     from awesome_acceleration_b200 import _lib, kernels as Kk
     from awesome_acceleration_b200.runtime import interleave_gate_up
-    if args.decode:
-        M = 32 if args.small else 256
-    else:
-        M = 8192 if args.small else 32768
+    M = 8192 if args.small else 32768
     H, I, hq, hkv = 1024, 3072, 16, 8
     g = torch.Generator(device=device).manual_seed(3)
     x = torch.randn((M, H), generator=g, device=device).to(torch.bfloat16)
@@ -762,6 +892,7 @@ def main():
     ap.add_argument("--no-tp-block", action="store_true",
                     help="cfg2: skip the cfg4 (Qwen3-8B) tensor-parallel block at TP = the world")
     ap.add_argument("--decode", action="store_true", help="gemm workload: decode-batch shapes")
+    ap.add_argument("--batch", type=int, default=0, help="gemm --decode: batch rows (default 256)")
     ap.add_argument("--midrun", action="store_true",
                     help="cfg2 profiler case: 1536-token prompts (the job's mean decode context), 7 decode steps")
     ap.add_argument("--profile", action="store_true",

@@ -185,6 +185,42 @@ int aacc_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, voi
 int aacc_gemm(const void* x, const void* w, void* out, int64_t M, int64_t N, int64_t K,
               cudaStream_t stream);
 
+/* ---- decode projections: cluster split-K with the epilogue fused ----------
+ * For decode-sized batches (1 <= M <= 256 rows; N % 128 == 0, K % 64 == 0).
+ * The K dimension of every 128-column output tile is split over the `splits`
+ * CTAs of one thread-block cluster; the fp32 partials are summed in split
+ * order through distributed shared memory (bit-identical to aacc_gemm_splitk
+ * + the split-K epilogue at the same split count) and the epilogue runs in
+ * the same kernel.  splits = 0 picks the split count (and 128- or 256-row
+ * tiles) so that all CTAs are resident at once.  One launch per projection,
+ * no workspace. */
+
+/* out[M][N] = bf16(x @ w^T): o_proj / down_proj of a decode step
+ * (model/model.py:237-238, :189-190), before the residual add + RMSNorm. */
+int aacc_gemm_cluster(const void* x, const void* w, void* out, int64_t M, int64_t N, int64_t K, int splits,
+                      cudaStream_t stream);
+
+/* out[M][I] = bf16(silu(bf16(gate))) * bf16(up) over gate/up rows
+ * interleaved by 64 (model/model.py:189-190), as aacc_gemm_silu_mul. */
+int aacc_gemm_silu_mul_cluster(const void* x, const void* w_gate_up, void* out, int64_t M, int64_t I, int64_t K,
+                               int splits, cudaStream_t stream);
+
+/* Fused QKV projection + q/k RMSNorm + RoPE + paged KV store of a decode
+ * step, as aacc_qkv_norm_rope_store (model/model.py:219-226, :233-240). */
+int aacc_qkv_norm_rope_store_cluster(const void* x, const void* w_qkv, const void* q_norm_w, const void* k_norm_w,
+                                     float eps, const int64_t* positions, const void* rope_cos_sin, int64_t max_pos,
+                                     const int64_t* slot_mapping, void* q_out, void* k_cache, void* v_cache,
+                                     int64_t num_blocks, int num_q_heads, int num_kv_heads, int block_size, int64_t M,
+                                     int64_t K, int splits, cudaStream_t stream);
+
+/* The plan splits = 0 selects for an M x N x K cluster GEMM on the current
+ * device: tile rows / 128 (1 or 2), tiles over M, and the split count. */
+int aacc_gemm_cluster_plan(int64_t M, int64_t N, int64_t K, int* mt, int* m_tiles, int* splits);
+
+/* CTAs of the cluster GEMM (tile rows / 128 = 1 or 2, clusters of `splits`)
+ * that fit on the current device at once (0 when none). */
+int64_t aacc_gemm_cluster_capacity(int tile_rows_128, int splits);
+
 /* out[M][N] = bf16(x[M][K] @ w[N][K]^T + bias[N]): the bias added in fp32
  * before the rounding, as a fused-bias F.linear does.  Column-parallel and
  * QKV-parallel layers built with bias=True (model/parallel_layers.py:72-89,

@@ -514,3 +514,74 @@ def test_tp_exchange_wait_runs_out_and_poisons(cuda):
     finally:
         K().tp_set_peer_wait_ms(20000)
         clear_err()
+
+
+# --------------------------------------------------------------------------- cluster split-K decode projections
+@pytest.mark.parametrize("M", [1, 37, 128, 129, 256])
+def test_cluster_gemms_equal_splitk_path(cuda, M):
+    """The cluster split-K kernels (partials summed in distributed shared memory,
+    epilogue fused) equal gemm_splitk + the split-K epilogue kernels bit for
+    bit at the same split count, for the QKV (norm + RoPE + KV store), SiLU
+    and bf16-store epilogues; the automatic plan stays within bf16 tolerance
+    of the unsplit GEMM."""
+    from awesome_acceleration_b200.runtime import interleave_gate_up, rope_table
+    g = torch.Generator().manual_seed(M)
+    H, I, hq, hkv, bs = 1024, 3072, 16, 8, 256
+    x = torch.randn((M, H), generator=g).to(BF).to(cuda)
+    a = torch.randn((M, I), generator=g).to(BF).to(cuda)
+    w = {n: (torch.randn(sh, generator=g) * 0.02).to(BF).to(cuda) for n, sh in
+         [("qkv", ((hq + 2 * hkv) * 128, H)), ("o", (H, hq * 128)), ("d", (H, I)), ("g", (I, H)), ("u", (I, H))]}
+    wgu = interleave_gate_up(w["g"], w["u"]).contiguous()
+    qn = (1 + 0.1 * torch.randn(128, generator=g)).to(BF).to(cuda)
+    kn = (1 + 0.1 * torch.randn(128, generator=g)).to(BF).to(cuda)
+    rope = rope_table(4096, 128, 1e6, cuda)
+    pos = torch.randint(0, 4096, (M,), generator=g).to(cuda)
+    nb = (M + bs - 1) // bs + 2
+    slots = torch.randperm(nb * bs, generator=g)[:M].to(cuda)
+    part = torch.empty(16 * M * 6144, dtype=torch.float32, device=cuda)
+    clear_err()
+    for splits in (1, 2, 4, 8):
+        # bf16 store (o / down)
+        for wt, inp in ((w["o"], a[:, :hq * 128].contiguous()), (w["d"], a)):
+            N, Kd = wt.shape
+            pv = part[:splits * M * N].view(splits, M, N)
+            K().gemm_splitk(inp, wt, pv, splits)
+            ref = torch.empty((M, N), dtype=BF, device=cuda)
+            K().splitk_reduce(pv, splits, ref)
+            out = K().gemm_cluster(inp, wt, splits=splits)
+            assert torch.equal(out, ref), f"store M={M} N={N} K={Kd} splits={splits}"
+        # SiLU-mul
+        pv = part[:splits * M * 2 * I].view(splits, M, 2 * I)
+        K().gemm_splitk(x, wgu, pv, splits)
+        ref = torch.empty((M, I), dtype=BF, device=cuda)
+        K().splitk_silu_mul(pv, splits, ref)
+        out = K().gemm_silu_mul_cluster(x, wgu, splits=splits)
+        assert torch.equal(out, ref), f"silu M={M} splits={splits}"
+        # QKV + q/k norm + RoPE + KV store
+        N = w["qkv"].shape[0]
+        pv = part[:splits * M * N].view(splits, M, N)
+        caches = []
+        for fused in (False, True):
+            kc = torch.zeros((nb, hkv, bs, 128), dtype=BF, device=cuda)
+            vc = torch.zeros_like(kc)
+            q = torch.zeros((M, hq, 128), dtype=BF, device=cuda)
+            if fused:
+                K().qkv_norm_rope_store_cluster(x, w["qkv"], qn, kn, 1e-6, pos, rope, slots, kc, vc, hq, q_out=q,
+                                                splits=splits)
+            else:
+                K().gemm_splitk(x, w["qkv"], pv, splits)
+                K().splitk_qkv_norm_rope_store(pv, splits, qn, kn, 1e-6, pos, rope, slots, kc, vc, hq, q)
+            caches.append((q, kc, vc))
+        for t0, t1 in zip(*caches):
+            assert torch.equal(t0, t1), f"qkv M={M} splits={splits}"
+    torch.cuda.synchronize()
+    assert dev_err() == 0
+    # automatic plan against the unsplit tcgen05 GEMM
+    plan = K().gemm_cluster_plan(M, H, I)
+    out = K().gemm_cluster(a, w["d"])
+    ref = K().gemm(a, w["d"])
+    err = (out.float() - ref.float()).abs().max().item()
+    assert err <= 1e-2 * ref.float().abs().max().item() + 1e-3, (plan, err)
+    caps = {(mt, s): K().gemm_cluster_capacity(mt, s) for mt in (1, 2) for s in (1, 2, 3, 4, 6, 8, 16)}
+    print(f"M={M}: plans qkv {K().gemm_cluster_plan(M, 4096, H)}, gate/up {K().gemm_cluster_plan(M, 2 * I, H)}, "
+          f"o {K().gemm_cluster_plan(M, H, 2048)}, down {plan}; resident CTAs per (tile rows/128, splits) {caps}")
