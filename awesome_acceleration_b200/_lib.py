@@ -36,6 +36,7 @@ SIGNATURES: dict[str, tuple] = {
                                                   I64, P]),
     "aacc_paged_decode_noalloc_capacity_bytes": (I64, []),
     "aacc_prefill_attention": (I32, [P, P, P, P, I64, P, I64, P, P, P, I64, I64, I32, I32, I32, F32, P]),
+    "aacc_prefill_attention_mma": (I32, [P, P, P, P, I64, P, I64, P, P, P, I64, I64, I32, I32, I32, F32, P]),
     "aacc_rmsnorm": (I32, [P, P, P, I64, I64, F32, P]),
     "aacc_add_rmsnorm": (I32, [P, P, P, P, I64, I64, F32, P]),
     "aacc_embed_rmsnorm": (I32, [P, P, I64, P, P, P, I64, I64, F32, P]),

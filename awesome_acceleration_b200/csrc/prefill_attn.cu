@@ -1,4 +1,7 @@
-// Causal (chunked) prefill attention over the paged KV cache.
+// Causal (chunked) prefill attention over the paged KV cache on mma.sync
+// (the legacy tensor-core path): aacc_prefill_attention_mma.  The engine's
+// path is the tcgen05 kernel in prefill_attn_tc.cu; this one serves block
+// sizes that are not multiples of 128 and A/B timing.
 //
 // One CTA per (64-query tile, query head, sequence).  The chunk's K/V (and
 // every earlier chunk of the same sequence) are already in the paged pool, so
@@ -225,7 +228,7 @@ using namespace aacc;
 
 extern "C" {
 
-int aacc_prefill_attention(const void* q, void* out, const void* k_cache, const void* v_cache, int64_t num_blocks,
+int aacc_prefill_attention_mma(const void* q, void* out, const void* k_cache, const void* v_cache, int64_t num_blocks,
                            const int32_t* block_tables, int64_t max_blocks, const int64_t* seq_rows, const int32_t* cu_q,
                            const int32_t* ctx_start, int64_t num_seqs, int64_t max_q_len, int num_q_heads,
                            int num_kv_heads, int block_size, float scale, cudaStream_t stream) {

@@ -1,0 +1,370 @@
+// Causal (chunked) prefill attention over the paged KV cache on tcgen05 /
+// TMEM: the B200 form of flash_attn_varlen_func (llm.py:178-184) for a chunk
+// whose K/V are already stored in the paged pool.
+//
+// One CTA per (query tile, kv head, sequence).  Its 128 MMA rows are the
+// 128 / G query positions of the tile times the G query heads that share the
+// kv head (row r = head g * P + position p, P = 128 / G), so every K/V byte
+// is read once per kv head, not once per query head.  Per 128-key tile:
+//
+//   producer warp   TMA: K and V tiles (two 64-column halves each, 128-byte
+//                   swizzle) from the paged pool into a 2-stage ring;
+//   MMA warp        S_i = Q K_i^T into one of two TMEM score buffers (so
+//                   S_{i+1} runs while the softmax reads S_i), then, once the
+//                   softmax has written P_i, O += P_i V_i into a TMEM
+//                   accumulator (V read as an MN-major operand, in place);
+//   softmax warps   one thread per row: S_i from TMEM, causal mask
+//                   key_pos <= query_pos (query p of the chunk sits at
+//                   ctx_start + tile start + p) on the tiles that cross the
+//                   diagonal, fp32 online softmax in base 2 (SFU exponential),
+//                   O rescaled in TMEM when a row's maximum grows, P_i rounded
+//                   to bf16 into shared memory (as FlashAttention-2 rounds P
+//                   before the PV product); at the end O / l to the output.
+//
+// Every wait is bounded; a wait that runs out reports ERR_WAIT_TIMEOUT and
+// the CTA stops issuing work, drains its own copies and frees TMEM.
+#include "common.cuh"
+#include "host.h"
+#include "tcgen05.cuh"
+
+namespace aacc {
+
+constexpr int kFD = 128;            // head dim
+constexpr int kFKeys = 128;         // keys per K/V tile
+constexpr int kFStages = 2;         // K/V ring depth
+constexpr int kFSoftmaxWarps = 4;   // one thread per MMA row
+constexpr int kFThreads = (kFSoftmaxWarps + 2) * 32;
+constexpr int kFHalf = 128 * 128;   // bytes of one 64-column half of a 128-row bf16 tile
+
+struct FlashSmem {
+  uint8_t kv[kFStages][4][kFHalf];  // per stage: K half 0, K half 1, V half 0, V half 1
+  uint8_t q[2][kFHalf];             // Q: 128 rows x 128 dims as two 64-dim halves
+  uint8_t p[2][kFHalf];             // P: 128 rows x 128 keys as two 64-key halves
+  uint64_t full[kFStages];
+  uint64_t empty[kFStages];
+  uint64_t s_full[2];
+  uint64_t p_full;
+  uint64_t pv_done;
+  uint32_t tmem_slot;
+  int abort;
+};
+
+// 2^x with the SFU's approximate exponential (PTX ex2.approx.ftz.f32); 2^-inf = 0.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int G>
+__global__ void __launch_bounds__(kFThreads, 1)
+    flash_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                         const bf16* __restrict__ q, bf16* __restrict__ out, const int32_t* __restrict__ bt,
+                         int64_t max_blocks, const int64_t* __restrict__ seq_rows, const int32_t* __restrict__ cu_q,
+                         const int32_t* __restrict__ ctx_start, int Hq, int Hkv, int bs, int64_t num_blocks,
+                         int n_qtiles, float scale_log2, unsigned* err) {
+  constexpr int P = 128 / G;  // query positions per CTA
+  extern __shared__ uint8_t smem_raw[];
+  FlashSmem& sm = *reinterpret_cast<FlashSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  griddep_wait();
+  griddep_launch();
+  const int qt = n_qtiles - 1 - (int)blockIdx.x;  // heaviest tiles first
+  const int kvh = blockIdx.y;
+  const int64_t s = blockIdx.z;
+  const int64_t q0 = cu_q[s];
+  const int q_len = cu_q[s + 1] - (int)q0;
+  const int qs = qt * P;
+  if (qs >= q_len) return;  // whole CTA, before any barrier or TMEM is set up
+  const int rows_here = min(P, q_len - qs);
+  const int64_t c0 = ctx_start[s];
+  const int64_t row = seq_rows[s];
+  const int64_t last_pos = c0 + qs + rows_here - 1;
+  int ntiles = (int)(last_pos / kFKeys) + 1;
+  if ((int64_t)ntiles * kFKeys > max_blocks * bs) {
+    if (threadIdx.x == 0) report(err, ERR_CTX_OOB);
+    ntiles = (int)(max_blocks * bs / kFKeys);
+  }
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kFStages; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], 1);
+    }
+    mbar_init(&sm.s_full[0], 1);
+    mbar_init(&sm.s_full[1], 1);
+    mbar_init(&sm.p_full, kFSoftmaxWarps * 32);
+    mbar_init(&sm.pv_done, 1);
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == kFSoftmaxWarps + 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm.tmem_slot)),
+                 "r"(512u)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (warp < kFSoftmaxWarps) {
+    // Q rows into shared memory (K-major, 128-byte swizzle): row r = head g * P + position p.
+    const int r = threadIdx.x, g = r / P, p = r % P;
+    const bool valid = p < rows_here;
+    const bf16* src = q + ((q0 + qs + (valid ? p : 0)) * Hq + (int64_t)kvh * G + g) * kFD;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      const uint4 v = valid ? reinterpret_cast<const uint4*>(src)[c] : make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(sm.q[c >> 3] + swz128(r, c & 7)) = v;
+    }
+    fence_proxy_async();  // the tensor core reads these generic-proxy writes
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_slot;
+  const uint32_t tS0 = tmem, tS1 = tmem + 128, tO = tmem + 256;
+  volatile int* abort = &sm.abort;
+
+  if (warp == kFSoftmaxWarps) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tmk);
+      tma_prefetch_desc(&tmv);
+      const int32_t* btrow = bt + row * max_blocks;
+      int issued = 0;
+      for (int i = 0; i < ntiles; ++i) {
+        const int st = i % kFStages;
+        if (i >= kFStages && !mbar_wait(&sm.empty[st], ((i / kFStages) - 1) & 1, err, abort)) break;
+        const int64_t t0 = (int64_t)i * kFKeys;
+        int64_t blk = btrow[t0 / bs];
+        if (blk < 0 || blk >= num_blocks) {
+          report(err, ERR_BLOCK_OOB);
+          blk = 0;
+        }
+        const int r = (int)((blk * Hkv + kvh) * bs + t0 % bs);
+        mbar_arrive_expect_tx(&sm.full[st], 4 * kFHalf);
+        tma_load_2d(sm.kv[st][0], &tmk, &sm.full[st], 0, r);
+        tma_load_2d(sm.kv[st][1], &tmk, &sm.full[st], 64, r);
+        tma_load_2d(sm.kv[st][2], &tmv, &sm.full[st], 0, r);
+        tma_load_2d(sm.kv[st][3], &tmv, &sm.full[st], 64, r);
+        ++issued;
+      }
+      for (int st = 0; st < kFStages && st < issued; ++st) {  // no copy in flight at exit
+        const int last = st + ((issued - 1 - st) / kFStages) * kFStages;
+        mbar_wait(&sm.full[st], (last / kFStages) & 1, err, nullptr);
+      }
+    }
+  } else if (warp == kFSoftmaxWarps + 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t id_s = umma_idesc_m128(kFKeys, false);  // S = Q K^T: both K-major (over dims)
+      constexpr uint32_t id_pv = umma_idesc_m128(kFD, true);     // O += P V: V is N(dims)-major
+      const uint32_t qb = smem_u32(sm.q[0]), pb = smem_u32(sm.p[0]);
+      auto issue_s = [&](int i) -> bool {
+        const int st = i % kFStages;
+        if (!mbar_wait(&sm.full[st], (i / kFStages) & 1, err, abort)) return false;
+        tc_fence_after();
+        const uint32_t kb = smem_u32(sm.kv[st][0]);
+        const uint32_t ts = (i & 1) ? tS1 : tS0;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // 16 dims per step
+          const uint32_t off = (uint32_t)((kk >> 2) * kFHalf + (kk & 3) * 32);
+          umma_bf16(ts, umma_desc_sw128(qb + off), umma_desc_sw128(kb + off), id_s, kk != 0);
+        }
+        umma_commit(&sm.s_full[i & 1]);
+        return true;
+      };
+      bool ok = ntiles > 0 && issue_s(0);
+      for (int i = 0; ok && i < ntiles; ++i) {
+        if (i + 1 < ntiles && !issue_s(i + 1)) break;
+        if (!mbar_wait(&sm.p_full, i & 1, err, abort)) break;
+        tc_fence_after();
+        const uint32_t vb = smem_u32(sm.kv[i % kFStages][2]);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // 16 keys per step
+          const uint64_t a = umma_desc_sw128(pb + (uint32_t)((kk >> 2) * kFHalf + (kk & 3) * 32));
+          const uint64_t b = umma_desc_sw128_mn(vb + (uint32_t)(kk * 16 * 128), kFHalf);
+          umma_bf16(tO, a, b, id_pv, (i | kk) != 0);
+        }
+        umma_commit(&sm.pv_done);
+        umma_commit(&sm.empty[i % kFStages]);  // K_i and V_i consumed
+      }
+    }
+  } else {
+    // ---------------- softmax warps: thread = row = TMEM lane ----------------
+    // Rows past the end of the chunk (p >= rows_here) are never stored and
+    // each MMA row is independent, so they need no masking: only tiles that
+    // cross the causal diagonal are masked.  The running maximum is kept on
+    // raw scores (the scale is positive), so each exponent is one FFMA + EX2.
+    const int r = threadIdx.x, p = r % P;
+    const bool row_valid = p < rows_here;
+    const int pos = (int)(c0 + qs + p), pos_min = (int)(c0 + qs);
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int i = 0; i < ntiles; ++i) {
+      if (!mbar_wait(&sm.s_full[i & 1], (i >> 1) & 1, err, abort)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t ts = ((i & 1) ? tS1 : tS0) + lane_off;
+      float sv[kFKeys];
+#pragma unroll
+      for (int c = 0; c < kFKeys / 32; ++c) {
+        float t[32];
+        tmem_ld32(ts + 32 * c, t);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sv[32 * c + j] = t[j];
+      }
+      const int k0 = i * kFKeys;
+      if (k0 + kFKeys - 1 > pos_min) {  // tile crosses the diagonal (warp-uniform)
+#pragma unroll
+        for (int j = 0; j < kFKeys; ++j)
+          if (k0 + j > pos) sv[j] = -INFINITY;
+      }
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int j = 0; j < kFKeys; j += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) mx[u] = fmaxf(mx[u], sv[j + u]);
+      }
+      const float m_new = fmaxf(m, fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])));
+      const float msc = (m_new == -INFINITY ? 0.f : m_new) * scale_log2;
+      const float alpha = fast_exp2(fmaf(m, scale_log2, -msc));  // m = -inf: 0
+      float rs[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < kFKeys; j += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          sv[j + u] = fast_exp2(fmaf(sv[j + u], scale_log2, -msc));
+          rs[u] += sv[j + u];
+        }
+      }
+      l = l * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+      m = m_new;
+      if (i > 0) {
+        // PV_{i-1} has finished with O and with the P buffer
+        if (!mbar_wait(&sm.pv_done, (i - 1) & 1, err, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {  // tcgen05.ld/st are warp-wide
+#pragma unroll 1
+          for (int c = 0; c < kFD / 16; ++c) {
+            float ov[16];
+            tmem_ld16(tO + lane_off + 16 * c, ov);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) ov[j] *= alpha;
+            tmem_st16(tO + lane_off + 16 * c, ov);
+          }
+          tmem_wait_st();
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {  // 8 keys per 16-byte chunk
+        uint4 v;
+        v.x = pack_bf16(sv[8 * c + 0], sv[8 * c + 1]);
+        v.y = pack_bf16(sv[8 * c + 2], sv[8 * c + 3]);
+        v.z = pack_bf16(sv[8 * c + 4], sv[8 * c + 5]);
+        v.w = pack_bf16(sv[8 * c + 6], sv[8 * c + 7]);
+        *reinterpret_cast<uint4*>(sm.p[c >> 3] + swz128(r, c & 7)) = v;
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      mbar_arrive(&sm.p_full);
+    }
+    // ---------------- epilogue: O / l ----------------
+    if (ok && ntiles > 0 && mbar_wait(&sm.pv_done, (ntiles - 1) & 1, err, abort)) {
+      tc_fence_after();
+      const float il = l > 0.f ? 1.f / l : 0.f;
+      const int g = r / P;
+      bf16* dst = out + ((q0 + qs + p) * Hq + (int64_t)kvh * G + g) * kFD;
+#pragma unroll 1
+      for (int c = 0; c < kFD / 16; ++c) {
+        float ov[16];
+        tmem_ld16(tO + lane_off + 16 * c, ov);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) ov[j] *= il;
+        if (row_valid) store16_bf16(dst + 16 * c, ov);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kFSoftmaxWarps + 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512u) : "memory");
+  }
+}
+
+}  // namespace aacc
+
+using namespace aacc;
+
+extern "C" int aacc_prefill_attention_mma(const void* q, void* out, const void* k_cache, const void* v_cache,
+                                          int64_t num_blocks, const int32_t* block_tables, int64_t max_blocks,
+                                          const int64_t* seq_rows, const int32_t* cu_q, const int32_t* ctx_start,
+                                          int64_t num_seqs, int64_t max_q_len, int num_q_heads, int num_kv_heads,
+                                          int block_size, float scale, cudaStream_t stream);
+
+namespace aacc {
+static bool prefill_use_mma() {
+  static const bool on = [] {
+    const char* v = getenv("AACC_PREFILL_ATTN");
+    return v && v[0] == 'm';
+  }();
+  return on;
+}
+}  // namespace aacc
+
+extern "C" {
+
+int aacc_prefill_attention(const void* q, void* out, const void* k_cache, const void* v_cache, int64_t num_blocks,
+                           const int32_t* block_tables, int64_t max_blocks, const int64_t* seq_rows, const int32_t* cu_q,
+                           const int32_t* ctx_start, int64_t num_seqs, int64_t max_q_len, int num_q_heads,
+                           int num_kv_heads, int block_size, float scale, cudaStream_t stream) {
+  if (num_seqs < 0 || max_q_len < 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads || block_size <= 0 ||
+      block_size % 64 || num_blocks <= 0 || max_blocks <= 0)
+    return set_error(AACC_ERR_INVALID, "prefill_attention: bad sizes");
+  const int G = num_q_heads / num_kv_heads;
+  // The tensor-core kernel takes 128-key tiles (block sizes that are multiples
+  // of 128) and 1, 2, 4 or 8 query heads per kv head; the mma.sync kernel
+  // covers 64-token blocks and other ratios.
+  if (block_size % kFKeys || (G != 1 && G != 2 && G != 4 && G != 8) || prefill_use_mma())
+    return aacc_prefill_attention_mma(q, out, k_cache, v_cache, num_blocks, block_tables, max_blocks, seq_rows, cu_q,
+                                      ctx_start, num_seqs, max_q_len, num_q_heads, num_kv_heads, block_size, scale,
+                                      stream);
+  if (num_seqs == 0 || max_q_len == 0) return AACC_OK;
+  if (num_seqs > 65535) return set_error(AACC_ERR_UNSUPPORTED, "prefill_attention: too many sequences per call");
+  const int64_t rows = num_blocks * num_kv_heads * block_size;
+  if (rows >= (int64_t(1) << 31)) return set_error(AACC_ERR_UNSUPPORTED, "prefill_attention: pool too large");
+  if (!aligned16(q) || !aligned16(out)) return set_error(AACC_ERR_INVALID, "prefill_attention: q/out must be 16-byte aligned");
+  CUtensorMap tmk, tmv;
+  int st = make_tmap_2d(&tmk, k_cache, kFD, rows, kFD * 2, 64, kFKeys, true);
+  if (st) return st;
+  st = make_tmap_2d(&tmv, v_cache, kFD, rows, kFD * 2, 64, kFKeys, true);
+  if (st) return st;
+  const int P = 128 / G;
+  const int n_qtiles = (int)((max_q_len + P - 1) / P);
+  const size_t smem = sizeof(FlashSmem) + 1024;
+  dim3 grid(n_qtiles, num_kv_heads, (unsigned)num_seqs);
+  cudaError_t le;
+#define AACC_LAUNCH_FLASH(GG)                                                                                      \
+  {                                                                                                                \
+    set_smem_once<flash_prefill_kernel<GG>>((int)smem);                                                            \
+    le = launch_k(flash_prefill_kernel<GG>, grid, dim3(kFThreads), smem, stream, tmk, tmv, (const bf16*)q,         \
+                  (bf16*)out, block_tables, max_blocks, seq_rows, cu_q, ctx_start, num_q_heads, num_kv_heads,       \
+                  block_size, num_blocks, n_qtiles, scale * kLog2e, device_error_ptr());                            \
+  }
+  switch (G) {
+    case 1: AACC_LAUNCH_FLASH(1) break;
+    case 2: AACC_LAUNCH_FLASH(2) break;
+    case 4: AACC_LAUNCH_FLASH(4) break;
+    default: AACC_LAUNCH_FLASH(8) break;
+  }
+#undef AACC_LAUNCH_FLASH
+  return check_launch("flash_prefill_kernel", le);
+}
+
+}  // extern "C"

@@ -392,6 +392,59 @@ def run_attn(args, device):
             "gpu_launches": 2 * args.steps, "clocks": clk.summary()}
 
 
+# --------------------------------------------------------------------------- prefill attention (tensor pipe)
+def run_prefill_attn(args, device):
+    """Causal prefill attention over the paged cache on one packed chunk of
+    the cfg2 prefill: 32 sequences x 1024 prompt tokens (32,768 query tokens),
+    16 / 8 heads, block 256, a permuted block pool.  FLOPs = 4 * 128 * Hq *
+    sum over queries of the keys each attends (causal).  AACC_PREFILL_ATTN=mma
+    times the mma.sync kernel instead of the tcgen05 one."""
+    from awesome_acceleration_b200 import _lib, kernels as Kk
+    n, L = (8, 1024) if args.small else (32, 1024)
+    hq, hkv, bs = 16, 8, 256
+    g = torch.Generator().manual_seed(11)
+    nb = n * (L // bs) + 8
+    perm = torch.randperm(nb, generator=g)
+    bt = perm[:n * (L // bs)].view(n, L // bs).int().to(device)
+    kc = torch.randn((nb, hkv, bs, 128), generator=g).to(torch.bfloat16).to(device)
+    vc = torch.randn((nb, hkv, bs, 128), generator=g).to(torch.bfloat16).to(device)
+    q = torch.randn((n * L, hq, 128), generator=g).to(torch.bfloat16).to(device)
+    rows = torch.arange(n, dtype=torch.int64, device=device)
+    cu = (torch.arange(n + 1, dtype=torch.int32) * L).to(device)
+    c0 = torch.zeros(n, dtype=torch.int32, device=device)
+    out = torch.empty_like(q)
+
+    def call():
+        Kk.prefill_attention(q, kc, vc, bt, rows, cu, c0, max_q_len=L, scale=128 ** -0.5, out=out)
+
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    ts = []
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        for _ in range(args.steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            call()
+            e1.record(stream)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1) / 1e3)
+    _lib.raise_on_device_error("prefill attention")
+    t = statistics.median(ts)
+    flops = 4 * 128 * hq * n * (L * (L + 1) // 2)
+    pk, kind = peaks()
+    ach = flops / t / 1e12
+    kernel = "mma.sync" if os.environ.get("AACC_PREFILL_ATTN", "").startswith("m") else "tcgen05"
+    return {"metric": f"causal prefill attention TFLOP/s ({n} x {L} tokens, 16/8 heads)", "value": round(ach, 1),
+            "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "cfg2 prefill chunk attention", "kernel": kernel, "l2": "K/V 1 GB > L2"},
+            "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": round(ach / pk["bf16_tflops"], 3), "traffic": None, "peak_kind": kind},
+            "gpu_launches": args.steps + args.warmup, "clocks": clk.summary()}
+
+
 # --------------------------------------------------------------------------- cfg4: Qwen3-8B tensor parallel
 QWEN3_8B_KW = dict(hidden_size=4096, intermediate_size=12288, num_hidden_layers=36, num_attention_heads=32,
                    num_key_value_heads=8, tie_word_embeddings=False)
@@ -885,7 +938,7 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg4", "cfg5", "attn", "gemm"])
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg4", "cfg5", "attn", "gemm", "prefill-attn"])
     ap.add_argument("--tp", type=int, default=0, help="cfg4/cfg5: tensor-parallel size (default: the whole world)")
     ap.add_argument("--small", action="store_true", help="small case for profiler captures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -912,8 +965,8 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                              device_id=device)
     try:
-        line = {"attn": run_attn, "gemm": run_gemm, "cfg2": run_cfg2, "cfg4": run_cfg4,
-                "cfg5": run_cfg5}[args.workload](args, device)
+        line = {"attn": run_attn, "gemm": run_gemm, "cfg2": run_cfg2, "cfg4": run_cfg4, "cfg5": run_cfg5,
+                "prefill-attn": run_prefill_attn}[args.workload](args, device)
         if args.workload == "cfg2" and not (args.small or args.profile or args.no_tp_block):
             import gc
             gc.collect()

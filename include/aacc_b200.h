@@ -139,6 +139,16 @@ int aacc_prefill_attention(const void* q, void* out, const void* k_cache, const 
                            int64_t num_seqs, int64_t max_q_len, int num_q_heads, int num_kv_heads,
                            int block_size, float scale, cudaStream_t stream);
 
+/* The same computation on mma.sync m16n8k16 with one CTA per query head
+ * (block_size % 64 == 0).  aacc_prefill_attention runs it for block sizes
+ * that are not multiples of 128; kept for A/B timing against the tcgen05
+ * kernel.  Replaces the same call (llm.py:178-184). */
+int aacc_prefill_attention_mma(const void* q, void* out, const void* k_cache, const void* v_cache,
+                               int64_t num_blocks, const int32_t* block_tables, int64_t max_blocks,
+                               const int64_t* seq_rows, const int32_t* cu_q, const int32_t* ctx_start,
+                               int64_t num_seqs, int64_t max_q_len, int num_q_heads, int num_kv_heads,
+                               int block_size, float scale, cudaStream_t stream);
+
 /* ---- RMSNorm ------------------------------------------------------------- */
 
 /* y = w * bf16(x * rsqrt(mean(x^2) + eps)), rows of `hidden` (multiple of

@@ -160,7 +160,7 @@ def test_paged_decode_attention(cuda, G, hkv):
 
 
 # --------------------------------------------------------------------------- prefill attention
-@pytest.mark.parametrize("G,hkv", [(2, 2), (4, 2), (1, 3)])
+@pytest.mark.parametrize("G,hkv", [(2, 2), (4, 2), (1, 3), (8, 1)])
 def test_prefill_attention_chunked(cuda, G, hkv):
     g = torch.Generator().manual_seed(20 + G)
     bs = 256
