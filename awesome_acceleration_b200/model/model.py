@@ -325,6 +325,19 @@ class Qwen3ForCausalLM(nn.Module):
             out.append({"k": k.to(device), "v": v.to(device), "seqlen": int(self.kv.lengths[int(slot_idx)])})
         return {"layers": out}
 
+    def export_request_kv_ipc(self, slot_idx: int, length: int):
+        """Hand a request's K/V to another process without host copies: returns
+        (ticket, owner); send the picklable ticket, call owner.release() once
+        the other side has imported it (awesome_acceleration_b200.kv_transfer)."""
+        from ..kv_transfer import export_request_kv_ipc
+        return export_request_kv_ipc(self, slot_idx, length)
+
+    def import_request_kv_ipc(self, slot_idx: int, ticket) -> None:
+        """Store a request exported by another process (export_request_kv_ipc)
+        into slot_idx, reading its device buffer in place (same GPU or NVLink)."""
+        from ..kv_transfer import import_request_kv_ipc
+        import_request_kv_ipc(self, slot_idx, ticket)
+
     def import_request_kv(self, slot_idx: int, payload: dict, length: int):
         """Write exported K/V into `slot_idx` (model/model.py:168-177, :392-401)."""
         layers = payload["layers"]
