@@ -392,6 +392,48 @@ def run_attn(args, device):
             "gpu_launches": 2 * args.steps, "clocks": clk.summary()}
 
 
+# --------------------------------------------------------------------------- HBM ceilings (context for the roofline)
+def run_hbm(args, device):
+    """Read-only and copy bandwidth of this GPU with library-independent torch
+    kernels: an int64 max-reduction over an 8 GB buffer (reads only) and a
+    2 GB copy (read + write, the form MEASURED_PEAKS.json's hbm_gbs takes).
+    The decode attention reads its KV stream once and writes little, so the
+    read-only figure is its practical ceiling."""
+    n = (1 if args.small else 4) * 1024 ** 3
+    x = torch.empty(n, dtype=torch.bfloat16, device=device)
+    x.normal_()
+    y = torch.empty(1024 ** 3 // (4 if args.small else 1), dtype=torch.bfloat16, device=device)
+    z = torch.empty_like(y)
+    stream = torch.cuda.current_stream()
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(args.steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1) / 1e3)
+        return statistics.median(ts)
+
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        t_read = timed(lambda: x.view(torch.int64).max())
+        t_copy = timed(lambda: z.copy_(y))
+    read_gbs = x.numel() * 2 / t_read / 1e9
+    copy_gbs = 2 * y.numel() * 2 / t_copy / 1e9
+    pk, kind = peaks()
+    return {"metric": "HBM read-only GB/s (int64 max over 8 GB)", "value": round(read_gbs, 1), "unit": "GB/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "HBM ceilings", "copy_gbs": round(copy_gbs, 1), "measured_peak_hbm_gbs": pk["hbm_gbs"],
+                       "peak_kind": kind, "l2": "buffers larger than L2"},
+            "gpu_launches": 0, "clocks": clk.summary()}
+
+
 # --------------------------------------------------------------------------- prefill attention (tensor pipe)
 def run_prefill_attn(args, device):
     """Causal prefill attention over the paged cache on one packed chunk of
@@ -938,7 +980,8 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg4", "cfg5", "attn", "gemm", "prefill-attn"])
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg4", "cfg5", "attn", "gemm", "prefill-attn",
+                                                             "hbm"])
     ap.add_argument("--tp", type=int, default=0, help="cfg4/cfg5: tensor-parallel size (default: the whole world)")
     ap.add_argument("--small", action="store_true", help="small case for profiler captures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -966,7 +1009,7 @@ def main():
                                              device_id=device)
     try:
         line = {"attn": run_attn, "gemm": run_gemm, "cfg2": run_cfg2, "cfg4": run_cfg4, "cfg5": run_cfg5,
-                "prefill-attn": run_prefill_attn}[args.workload](args, device)
+                "prefill-attn": run_prefill_attn, "hbm": run_hbm}[args.workload](args, device)
         if args.workload == "cfg2" and not (args.small or args.profile or args.no_tp_block):
             import gc
             gc.collect()
