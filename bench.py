@@ -732,12 +732,13 @@ def run_decode_projections(args, device):
         return (torch.randn(shape, generator=g, device=device) * std).to(torch.bfloat16)
 
     layers = []
-    for _ in range(L):
+    for _ in range(1 if args.hot_weights else L):
         layers.append({"qkv": rnd((hq + 2 * hkv) * 128, H), "o": rnd(H, hq * 128),
                        "gu": interleave_gate_up(rnd(I, H), rnd(I, H)).contiguous(), "d": rnd(H, I),
                        "qn": torch.ones(128, dtype=torch.bfloat16, device=device),
                        "kn": torch.ones(128, dtype=torch.bfloat16, device=device),
                        "ln": torch.ones(H, dtype=torch.bfloat16, device=device)})
+    layers = layers * (L // len(layers))  # --hot-weights: one layer's weights 28 times (L2-resident)
     x, res = rnd(B, H, std=1.0), rnd(B, H, std=1.0)
     attn, act, delta = rnd(B, hq * 128, std=1.0), rnd(B, I, std=1.0), rnd(B, H)
     q = torch.empty((B, hq, 128), dtype=torch.bfloat16, device=device)
@@ -834,7 +835,9 @@ def run_decode_projections(args, device):
     return {"metric": f"decode projections us per layer (Qwen3-0.6B shapes, B={B})", "value": res_us["cluster.layer"],
             "unit": "us per layer", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "decode projections of one layer, 28 layers of distinct weights per graph",
+            "config": {"workload": "decode projections of one layer, " + (
+                           "one layer's weights 28 times (L2-resident)" if args.hot_weights
+                           else "28 layers of distinct weights per graph"),
                        "per_variant_us": res_us, "cluster_plans (mt, m_tiles, splits)": plans,
                        "l2": "weights 840 MB > L2"},
             "roofline": {"bound": "hbm", "achieved": round(w_layer / t / 1e9, 1), "peak": pk["hbm_gbs"],
@@ -989,6 +992,8 @@ def main():
                     help="cfg2: skip the cfg4 (Qwen3-8B) tensor-parallel block at TP = the world")
     ap.add_argument("--decode", action="store_true", help="gemm workload: decode-batch shapes")
     ap.add_argument("--batch", type=int, default=0, help="gemm --decode: batch rows (default 256)")
+    ap.add_argument("--hot-weights", action="store_true",
+                    help="gemm --decode: reuse one layer's weights (L2-resident) to bound what prefetching could gain")
     ap.add_argument("--midrun", action="store_true",
                     help="cfg2 profiler case: 1536-token prompts (the job's mean decode context), 7 decode steps")
     ap.add_argument("--profile", action="store_true",
