@@ -2,24 +2,28 @@
 // TMEM: the B200 form of flash_attn_varlen_func (llm.py:178-184) for a chunk
 // whose K/V are already stored in the paged pool.
 //
-// One CTA per (query tile, kv head, sequence).  Its 128 MMA rows are the
-// 128 / G query positions of the tile times the G query heads that share the
-// kv head (row r = head g * P + position p, P = 128 / G), so every K/V byte
-// is read once per kv head, not once per query head.  Per 128-key tile:
+// One CTA per (pair of query tiles, kv head, sequence).  A tile's 128 MMA
+// rows are 128 / G query positions times the G query heads that share the kv
+// head (row r = head g * P + position p, P = 128 / G), so every K/V byte is
+// read once per kv head, not once per query head; the two tiles (A: positions
+// [qs, qs + P), B: the next P) share every K/V tile.  Per 128-key tile:
 //
 //   producer warp   TMA: K and V tiles (two 64-column halves each, 128-byte
 //                   swizzle) from the paged pool into a 2-stage ring;
-//   MMA warp        S_i = Q K_i^T into one of two TMEM score buffers (so
-//                   S_{i+1} runs while the softmax reads S_i), then, once the
-//                   softmax has written P_i, O += P_i V_i into a TMEM
-//                   accumulator (V read as an MN-major operand, in place);
-//   softmax warps   one thread per row: S_i from TMEM, causal mask
-//                   key_pos <= query_pos (query p of the chunk sits at
+//   MMA warp        S_t = Q_t K^T into tile t's TMEM score columns, and, once
+//                   tile t's softmax group has written P, O_t += P V into its
+//                   TMEM accumulator (V read as an MN-major operand, in
+//                   place), in the order S_A S_B | PV_A S_A' PV_B S_B' | ...
+//                   so one group's softmax overlaps the other's MMAs;
+//   softmax groups  4 warps per tile, one thread per row: S from TMEM, causal
+//                   mask key_pos <= query_pos (query p of the chunk sits at
 //                   ctx_start + tile start + p) on the tiles that cross the
 //                   diagonal, fp32 online softmax in base 2 (SFU exponential),
-//                   O rescaled in TMEM when a row's maximum grows, P_i rounded
-//                   to bf16 into shared memory (as FlashAttention-2 rounds P
-//                   before the PV product); at the end O / l to the output.
+//                   O rescaled in TMEM when a row's maximum grows, P rounded
+//                   to bf16 into the shared P buffer (as FlashAttention-2
+//                   rounds P before the PV product); at the end O / l out.
+//
+// TMEM: S_A | S_B | O_A | O_B (128 columns each).
 //
 // Every wait is bounded; a wait that runs out reports ERR_WAIT_TIMEOUT and
 // the CTA stops issuing work, drains its own copies and frees TMEM.
@@ -32,19 +36,20 @@ namespace aacc {
 constexpr int kFD = 128;            // head dim
 constexpr int kFKeys = 128;         // keys per K/V tile
 constexpr int kFStages = 2;         // K/V ring depth
-constexpr int kFSoftmaxWarps = 4;   // one thread per MMA row
+constexpr int kFGroupWarps = 4;     // one softmax group: a thread per MMA row of one query tile
+constexpr int kFSoftmaxWarps = 2 * kFGroupWarps;
 constexpr int kFThreads = (kFSoftmaxWarps + 2) * 32;
 constexpr int kFHalf = 128 * 128;   // bytes of one 64-column half of a 128-row bf16 tile
 
 struct FlashSmem {
   uint8_t kv[kFStages][4][kFHalf];  // per stage: K half 0, K half 1, V half 0, V half 1
-  uint8_t q[2][kFHalf];             // Q: 128 rows x 128 dims as two 64-dim halves
-  uint8_t p[2][kFHalf];             // P: 128 rows x 128 keys as two 64-key halves
+  uint8_t q[2][2][kFHalf];          // two query tiles: 128 rows x 128 dims as two 64-dim halves
+  uint8_t p[2][kFHalf];             // P: 128 rows x 128 keys, shared by the two tiles in turn
   uint64_t full[kFStages];
   uint64_t empty[kFStages];
-  uint64_t s_full[2];
-  uint64_t p_full;
-  uint64_t pv_done;
+  uint64_t s_full[2];               // per tile: S ready
+  uint64_t p_full[2];               // per tile: P written, O corrected
+  uint64_t pv_done[2];              // per tile: O += P V done
   uint32_t tmem_slot;
   int abort;
 };
@@ -62,28 +67,34 @@ __global__ void __launch_bounds__(kFThreads, 1)
                          const bf16* __restrict__ q, bf16* __restrict__ out, const int32_t* __restrict__ bt,
                          int64_t max_blocks, const int64_t* __restrict__ seq_rows, const int32_t* __restrict__ cu_q,
                          const int32_t* __restrict__ ctx_start, int Hq, int Hkv, int bs, int64_t num_blocks,
-                         int n_qtiles, float scale_log2, unsigned* err) {
-  constexpr int P = 128 / G;  // query positions per CTA
+                         int n_pairs, float scale_log2, unsigned* err) {
+  constexpr int P = 128 / G;  // query positions per tile
   extern __shared__ uint8_t smem_raw[];
   FlashSmem& sm = *reinterpret_cast<FlashSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   griddep_wait();
   griddep_launch();
-  const int qt = n_qtiles - 1 - (int)blockIdx.x;  // heaviest tiles first
+  const int pair = n_pairs - 1 - (int)blockIdx.x;  // heaviest tiles first
   const int kvh = blockIdx.y;
   const int64_t s = blockIdx.z;
   const int64_t q0 = cu_q[s];
   const int q_len = cu_q[s + 1] - (int)q0;
-  const int qs = qt * P;
-  if (qs >= q_len) return;  // whole CTA, before any barrier or TMEM is set up
-  const int rows_here = min(P, q_len - qs);
+  const int qs0 = pair * 2 * P;  // tile A: positions [qs0, qs0 + P); tile B: the next P
+  if (qs0 >= q_len) return;      // whole CTA, before any barrier or TMEM is set up
   const int64_t c0 = ctx_start[s];
   const int64_t row = seq_rows[s];
-  const int64_t last_pos = c0 + qs + rows_here - 1;
-  int ntiles = (int)(last_pos / kFKeys) + 1;
-  if ((int64_t)ntiles * kFKeys > max_blocks * bs) {
+  const int64_t kv_cap = max_blocks * bs / kFKeys;  // key tiles the block table can hold
+  // rows and key tiles of tile A (a) and tile B (b)
+  const int rows_a = min(P, q_len - qs0);
+  const int rows_b = qs0 + P < q_len ? min(P, q_len - qs0 - P) : 0;
+  int nt_a = (int)((c0 + qs0 + rows_a - 1) / kFKeys) + 1;
+  int nt_b = rows_b ? (int)((c0 + qs0 + P + rows_b - 1) / kFKeys) + 1 : 0;
+  if (nt_a > kv_cap || nt_b > kv_cap) {
     if (threadIdx.x == 0) report(err, ERR_CTX_OOB);
-    ntiles = (int)(max_blocks * bs / kFKeys);
+    nt_a = min(nt_a, (int)kv_cap);
+    nt_b = min(nt_b, (int)kv_cap);
   }
+  const bool have_b = nt_b > 0;
+  const int nkv = max(nt_a, nt_b);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -91,10 +102,11 @@ __global__ void __launch_bounds__(kFThreads, 1)
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], 1);
     }
-    mbar_init(&sm.s_full[0], 1);
-    mbar_init(&sm.s_full[1], 1);
-    mbar_init(&sm.p_full, kFSoftmaxWarps * 32);
-    mbar_init(&sm.pv_done, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&sm.s_full[t], 1);
+      mbar_init(&sm.p_full[t], kFGroupWarps * 32);
+      mbar_init(&sm.pv_done[t], 1);
+    }
     sm.abort = 0;
     fence_mbar_init();
   }
@@ -105,22 +117,22 @@ __global__ void __launch_bounds__(kFThreads, 1)
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (warp < kFSoftmaxWarps) {
-    // Q rows into shared memory (K-major, 128-byte swizzle): row r = head g * P + position p.
-    const int r = threadIdx.x, g = r / P, p = r % P;
-    const bool valid = p < rows_here;
-    const bf16* src = q + ((q0 + qs + (valid ? p : 0)) * Hq + (int64_t)kvh * G + g) * kFD;
+    // Q rows of this group's tile into shared memory (K-major, 128-byte
+    // swizzle): row r = head g * P + position p.
+    const int t = warp / kFGroupWarps, r = threadIdx.x % 128, g = r / P, p = r % P;
+    const bool valid = p < (t ? rows_b : rows_a);
+    const bf16* src = q + ((q0 + qs0 + t * P + (valid ? p : 0)) * Hq + (int64_t)kvh * G + g) * kFD;
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
       const uint4 v = valid ? reinterpret_cast<const uint4*>(src)[c] : make_uint4(0, 0, 0, 0);
-      *reinterpret_cast<uint4*>(sm.q[c >> 3] + swz128(r, c & 7)) = v;
+      *reinterpret_cast<uint4*>(sm.q[t][c >> 3] + swz128(r, c & 7)) = v;
     }
     fence_proxy_async();  // the tensor core reads these generic-proxy writes
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = sm.tmem_slot;
-  const uint32_t tS0 = tmem, tS1 = tmem + 128, tO = tmem + 256;
+  const uint32_t tmem = sm.tmem_slot;  // S_A | S_B | O_A | O_B, 128 columns each
   volatile int* abort = &sm.abort;
 
   if (warp == kFSoftmaxWarps) {
@@ -130,7 +142,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
       tma_prefetch_desc(&tmv);
       const int32_t* btrow = bt + row * max_blocks;
       int issued = 0;
-      for (int i = 0; i < ntiles; ++i) {
+      for (int i = 0; i < nkv; ++i) {
         const int st = i % kFStages;
         if (i >= kFStages && !mbar_wait(&sm.empty[st], ((i / kFStages) - 1) & 1, err, abort)) break;
         const int64_t t0 = (int64_t)i * kFKeys;
@@ -154,66 +166,83 @@ __global__ void __launch_bounds__(kFThreads, 1)
     }
   } else if (warp == kFSoftmaxWarps + 1) {
     // ---------------- MMA issuer ----------------
+    // Tensor-pipe order: S_A(0) S_B(0) | PV_A(i) S_A(i+1) PV_B(i) S_B(i+1) | ...
+    // so each group's softmax overlaps the other group's MMAs.
     if (lane == 0) {
       constexpr uint32_t id_s = umma_idesc_m128(kFKeys, false);  // S = Q K^T: both K-major (over dims)
       constexpr uint32_t id_pv = umma_idesc_m128(kFD, true);     // O += P V: V is N(dims)-major
-      const uint32_t qb = smem_u32(sm.q[0]), pb = smem_u32(sm.p[0]);
-      auto issue_s = [&](int i) -> bool {
-        const int st = i % kFStages;
-        if (!mbar_wait(&sm.full[st], (i / kFStages) & 1, err, abort)) return false;
-        tc_fence_after();
-        const uint32_t kb = smem_u32(sm.kv[st][0]);
-        const uint32_t ts = (i & 1) ? tS1 : tS0;
+      const uint32_t pb = smem_u32(sm.p[0]);
+      auto issue_s = [&](int t, int i) {
+        const uint32_t qb = smem_u32(sm.q[t][0]), kb = smem_u32(sm.kv[i % kFStages][0]);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // 16 dims per step
           const uint32_t off = (uint32_t)((kk >> 2) * kFHalf + (kk & 3) * 32);
-          umma_bf16(ts, umma_desc_sw128(qb + off), umma_desc_sw128(kb + off), id_s, kk != 0);
+          umma_bf16(tmem + 128 * t, umma_desc_sw128(qb + off), umma_desc_sw128(kb + off), id_s, kk != 0);
         }
-        umma_commit(&sm.s_full[i & 1]);
-        return true;
+        umma_commit(&sm.s_full[t]);
       };
-      bool ok = ntiles > 0 && issue_s(0);
-      for (int i = 0; ok && i < ntiles; ++i) {
-        if (i + 1 < ntiles && !issue_s(i + 1)) break;
-        if (!mbar_wait(&sm.p_full, i & 1, err, abort)) break;
+      auto issue_pv = [&](int t, int i) -> bool {
+        if (!mbar_wait(&sm.p_full[t], i & 1, err, abort)) return false;
         tc_fence_after();
         const uint32_t vb = smem_u32(sm.kv[i % kFStages][2]);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // 16 keys per step
           const uint64_t a = umma_desc_sw128(pb + (uint32_t)((kk >> 2) * kFHalf + (kk & 3) * 32));
           const uint64_t b = umma_desc_sw128_mn(vb + (uint32_t)(kk * 16 * 128), kFHalf);
-          umma_bf16(tO, a, b, id_pv, (i | kk) != 0);
+          umma_bf16(tmem + 256 + 128 * t, a, b, id_pv, (i | kk) != 0);
         }
-        umma_commit(&sm.pv_done);
+        umma_commit(&sm.pv_done[t]);
+        return true;
+      };
+      auto wait_full = [&](int i) -> bool {
+        if (!mbar_wait(&sm.full[i % kFStages], (i / kFStages) & 1, err, abort)) return false;
+        tc_fence_after();
+        return true;
+      };
+      bool ok = nkv > 0 && wait_full(0);
+      if (ok) {
+        if (nt_a > 0) issue_s(0, 0);
+        if (have_b) issue_s(1, 0);
+      }
+      for (int i = 0; ok && i < nkv; ++i) {
+        const bool more = i + 1 < nkv;
+        if (i < nt_a && !(ok = issue_pv(0, i))) break;
+        if (more && !(ok = wait_full(i + 1))) break;
+        if (i + 1 < nt_a) issue_s(0, i + 1);
+        if (have_b && i < nt_b && !(ok = issue_pv(1, i))) break;
+        if (have_b && i + 1 < nt_b) issue_s(1, i + 1);
         umma_commit(&sm.empty[i % kFStages]);  // K_i and V_i consumed
       }
     }
   } else {
-    // ---------------- softmax warps: thread = row = TMEM lane ----------------
-    // Rows past the end of the chunk (p >= rows_here) are never stored and
-    // each MMA row is independent, so they need no masking: only tiles that
-    // cross the causal diagonal are masked.  The running maximum is kept on
-    // raw scores (the scale is positive), so each exponent is one FFMA + EX2.
-    const int r = threadIdx.x, p = r % P;
+    // ---------------- softmax groups: group t = tile t, thread = row = TMEM lane ----------------
+    // Rows past the end of the chunk are never stored and each MMA row is
+    // independent, so they need no masking: only tiles that cross the causal
+    // diagonal are masked.  The running maximum is kept on raw scores (the
+    // scale is positive), so each exponent is one FFMA + EX2.  The P buffer
+    // is shared: the writes alternate A(0) B(0) A(1) B(1) ..., each after the
+    // previous P.V has finished reading it.
+    const int t = warp / kFGroupWarps, r = threadIdx.x % 128, p = r % P;
+    const int qs = qs0 + t * P, rows_here = t ? rows_b : rows_a, ntiles = t ? nt_b : nt_a;
     const bool row_valid = p < rows_here;
     const int pos = (int)(c0 + qs + p), pos_min = (int)(c0 + qs);
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_off = (uint32_t)((warp % kFGroupWarps) * 32) << 16;
+    const uint32_t tS = tmem + 128 * t, tO = tmem + 256 + 128 * t;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int i = 0; i < ntiles; ++i) {
-      if (!mbar_wait(&sm.s_full[i & 1], (i >> 1) & 1, err, abort)) {
+      if (!mbar_wait(&sm.s_full[t], i & 1, err, abort)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t ts = ((i & 1) ? tS1 : tS0) + lane_off;
       float sv[kFKeys];
 #pragma unroll
       for (int c = 0; c < kFKeys / 32; ++c) {
-        float t[32];
-        tmem_ld32(ts + 32 * c, t);
+        float tv[32];
+        tmem_ld32(tS + lane_off + 32 * c, tv);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) sv[32 * c + j] = t[j];
+        for (int j = 0; j < 32; ++j) sv[32 * c + j] = tv[j];
       }
       const int k0 = i * kFKeys;
       if (k0 + kFKeys - 1 > pos_min) {  // tile crosses the diagonal (warp-uniform)
@@ -241,24 +270,39 @@ __global__ void __launch_bounds__(kFThreads, 1)
       }
       l = l * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
       m = m_new;
-      if (i > 0) {
-        // PV_{i-1} has finished with O and with the P buffer
-        if (!mbar_wait(&sm.pv_done, (i - 1) & 1, err, abort)) {
+      // The P.V issued just before this one (the other tile's at the same
+      // step, or this tile's previous) must be done: it reads the shared P
+      // buffer, and it follows this tile's own previous P.V, which updates O.
+      int wt = -1, wi = 0;
+      if (t == 0 && i > 0) {
+        wt = have_b ? 1 : 0;
+        wi = i - 1;
+      } else if (t == 1) {
+        if (i < nt_a) {
+          wt = 0;
+          wi = i;
+        } else if (i > 0) {
+          wt = 1;
+          wi = i - 1;
+        }
+      }
+      if (wt >= 0) {
+        if (!mbar_wait(&sm.pv_done[wt], wi & 1, err, abort)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {  // tcgen05.ld/st are warp-wide
+      }
+      if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {  // tcgen05.ld/st are warp-wide
 #pragma unroll 1
-          for (int c = 0; c < kFD / 16; ++c) {
-            float ov[16];
-            tmem_ld16(tO + lane_off + 16 * c, ov);
+        for (int c = 0; c < kFD / 16; ++c) {
+          float ov[16];
+          tmem_ld16(tO + lane_off + 16 * c, ov);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) ov[j] *= alpha;
-            tmem_st16(tO + lane_off + 16 * c, ov);
-          }
-          tmem_wait_st();
+          for (int j = 0; j < 16; ++j) ov[j] *= alpha;
+          tmem_st16(tO + lane_off + 16 * c, ov);
         }
+        tmem_wait_st();
       }
 #pragma unroll
       for (int c = 0; c < 16; ++c) {  // 8 keys per 16-byte chunk
@@ -271,10 +315,10 @@ __global__ void __launch_bounds__(kFThreads, 1)
       }
       fence_proxy_async();
       tc_fence_before();
-      mbar_arrive(&sm.p_full);
+      mbar_arrive(&sm.p_full[t]);
     }
     // ---------------- epilogue: O / l ----------------
-    if (ok && ntiles > 0 && mbar_wait(&sm.pv_done, (ntiles - 1) & 1, err, abort)) {
+    if (ok && ntiles > 0 && mbar_wait(&sm.pv_done[t], (ntiles - 1) & 1, err, abort)) {
       tc_fence_after();
       const float il = l > 0.f ? 1.f / l : 0.f;
       const int g = r / P;
@@ -346,16 +390,16 @@ int aacc_prefill_attention(const void* q, void* out, const void* k_cache, const 
   st = make_tmap_2d(&tmv, v_cache, kFD, rows, kFD * 2, 64, kFKeys, true);
   if (st) return st;
   const int P = 128 / G;
-  const int n_qtiles = (int)((max_q_len + P - 1) / P);
+  const int n_pairs = (int)((max_q_len + 2 * P - 1) / (2 * P));
   const size_t smem = sizeof(FlashSmem) + 1024;
-  dim3 grid(n_qtiles, num_kv_heads, (unsigned)num_seqs);
+  dim3 grid(n_pairs, num_kv_heads, (unsigned)num_seqs);
   cudaError_t le;
 #define AACC_LAUNCH_FLASH(GG)                                                                                      \
   {                                                                                                                \
     set_smem_once<flash_prefill_kernel<GG>>((int)smem);                                                            \
     le = launch_k(flash_prefill_kernel<GG>, grid, dim3(kFThreads), smem, stream, tmk, tmv, (const bf16*)q,         \
                   (bf16*)out, block_tables, max_blocks, seq_rows, cu_q, ctx_start, num_q_heads, num_kv_heads,       \
-                  block_size, num_blocks, n_qtiles, scale * kLog2e, device_error_ptr());                            \
+                  block_size, num_blocks, n_pairs, scale * kLog2e, device_error_ptr());                            \
   }
   switch (G) {
     case 1: AACC_LAUNCH_FLASH(1) break;
