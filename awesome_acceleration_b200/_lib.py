@@ -50,6 +50,10 @@ SIGNATURES: dict[str, tuple] = {
                                                I32, P]),
     "aacc_gemm_cluster_plan": (I32, [I64, I64, I64, P, P, P]),
     "aacc_gemm_cluster_capacity": (I64, [I32, I32]),
+    "aacc_gemm_skinny_splitk": (I32, [P, P, P, I64, I64, I64, I32, P]),
+    "aacc_skinny_qkv_norm_rope_store": (I32, [P, P, P, I32, P, P, P, F32, P, P, I64, P, P, P, P, I64, I32, I32, I32,
+                                              I64, I64, P]),
+    "aacc_skinny_silu_mul": (I32, [P, P, P, I32, P, P, I64, I64, I64, P]),
     "aacc_bias_add": (I32, [P, P, I64, I64, P]),
     "aacc_splitk_add_rmsnorm": (I32, [P, I32, P, P, P, I64, I64, F32, P]),
     "aacc_splitk_reduce": (I32, [P, I32, P, I64, I64, P]),

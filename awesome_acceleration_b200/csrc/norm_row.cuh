@@ -67,7 +67,7 @@ __device__ __forceinline__ void load_row(float (&x)[V * 8], const bf16* __restri
 __device__ __forceinline__ void sum_partials8(const float* __restrict__ part, int S, int64_t split_stride, float (&d)[8]) {
   float4 a = reinterpret_cast<const float4*>(part)[0], b = reinterpret_cast<const float4*>(part)[1];
   d[0] = a.x; d[1] = a.y; d[2] = a.z; d[3] = a.w; d[4] = b.x; d[5] = b.y; d[6] = b.z; d[7] = b.w;
-#pragma unroll 4
+#pragma unroll 8
   for (int s = 1; s < S; ++s) {
     a = reinterpret_cast<const float4*>(part + s * split_stride)[0];
     b = reinterpret_cast<const float4*>(part + s * split_stride)[1];

@@ -9,7 +9,9 @@
 // [qs, qs + P), B: the next P) share every K/V tile.  Per 128-key tile:
 //
 //   producer warp   TMA: K and V tiles (two 64-column halves each, 128-byte
-//                   swizzle) from the paged pool into a 2-stage ring;
+//                   swizzle) from the paged pool into a ring of three 32 KB
+//                   slots, in the order K0 V0 K1 V1 ...: a K slot is free
+//                   once both tiles' S used it, a V slot once both P.V did;
 //   MMA warp        S_t = Q_t K^T into tile t's TMEM score columns, and, once
 //                   tile t's softmax group has written P, O_t += P V into its
 //                   TMEM accumulator (V read as an MN-major operand, in
@@ -19,9 +21,14 @@
 //                   mask key_pos <= query_pos (query p of the chunk sits at
 //                   ctx_start + tile start + p) on the tiles that cross the
 //                   diagonal, fp32 online softmax in base 2 (SFU exponential),
-//                   O rescaled in TMEM when a row's maximum grows, P rounded
-//                   to bf16 into the shared P buffer (as FlashAttention-2
-//                   rounds P before the PV product); at the end O / l out.
+//                   P rounded to bf16 into the tile's own P buffer (as
+//                   FlashAttention-2 rounds P before the PV product), so
+//                   neither group waits for the other's P.V; at the
+//                   end O / l out.  The reference maximum of a row moves only
+//                   when the row's running maximum exceeds it by more than
+//                   2^8 (in exp2 units, as FlashAttention-4 does): P stays
+//                   <= 256, O / l is the same quotient, and the O rescale in
+//                   TMEM (a read-modify-write on the critical path) is rare.
 //
 // TMEM: S_A | S_B | O_A | O_B (128 columns each).
 //
@@ -35,18 +42,19 @@ namespace aacc {
 
 constexpr int kFD = 128;            // head dim
 constexpr int kFKeys = 128;         // keys per K/V tile
-constexpr int kFStages = 2;         // K/V ring depth
+constexpr int kFSlots = 3;          // K/V ring: 32 KB slots holding K0 V0 K1 V1 ...
 constexpr int kFGroupWarps = 4;     // one softmax group: a thread per MMA row of one query tile
 constexpr int kFSoftmaxWarps = 2 * kFGroupWarps;
 constexpr int kFThreads = (kFSoftmaxWarps + 2) * 32;
 constexpr int kFHalf = 128 * 128;   // bytes of one 64-column half of a 128-row bf16 tile
+constexpr float kFRescaleLog2 = 8.f;  // move a row's reference maximum when exp2 would exceed 2^8
 
 struct FlashSmem {
-  uint8_t kv[kFStages][4][kFHalf];  // per stage: K half 0, K half 1, V half 0, V half 1
+  uint8_t kv[kFSlots][2][kFHalf];   // a K or V tile: 128 keys x 128 dims as two 64-dim halves
   uint8_t q[2][2][kFHalf];          // two query tiles: 128 rows x 128 dims as two 64-dim halves
-  uint8_t p[2][kFHalf];             // P: 128 rows x 128 keys, shared by the two tiles in turn
-  uint64_t full[kFStages];
-  uint64_t empty[kFStages];
+  uint8_t p[2][2][kFHalf];          // per tile, P: 128 rows x 128 keys as two 64-key halves
+  uint64_t full[kFSlots];
+  uint64_t empty[kFSlots];
   uint64_t s_full[2];               // per tile: S ready
   uint64_t p_full[2];               // per tile: P written, O corrected
   uint64_t pv_done[2];              // per tile: O += P V done
@@ -98,7 +106,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kFStages; ++i) {
+    for (int i = 0; i < kFSlots; ++i) {
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], 1);
     }
@@ -141,39 +149,44 @@ __global__ void __launch_bounds__(kFThreads, 1)
       tma_prefetch_desc(&tmk);
       tma_prefetch_desc(&tmv);
       const int32_t* btrow = bt + row * max_blocks;
+      // unit u: K (u even) or V (u odd) of key tile u / 2, into slot u % 3
       int issued = 0;
-      for (int i = 0; i < nkv; ++i) {
-        const int st = i % kFStages;
-        if (i >= kFStages && !mbar_wait(&sm.empty[st], ((i / kFStages) - 1) & 1, err, abort)) break;
-        const int64_t t0 = (int64_t)i * kFKeys;
+      for (int u = 0; u < 2 * nkv; ++u) {
+        const int sl = u % kFSlots;
+        if (u >= kFSlots && !mbar_wait(&sm.empty[sl], ((u / kFSlots) - 1) & 1, err, abort)) break;
+        const int64_t t0 = (int64_t)(u >> 1) * kFKeys;
         int64_t blk = btrow[t0 / bs];
         if (blk < 0 || blk >= num_blocks) {
           report(err, ERR_BLOCK_OOB);
           blk = 0;
         }
         const int r = (int)((blk * Hkv + kvh) * bs + t0 % bs);
-        mbar_arrive_expect_tx(&sm.full[st], 4 * kFHalf);
-        tma_load_2d(sm.kv[st][0], &tmk, &sm.full[st], 0, r);
-        tma_load_2d(sm.kv[st][1], &tmk, &sm.full[st], 64, r);
-        tma_load_2d(sm.kv[st][2], &tmv, &sm.full[st], 0, r);
-        tma_load_2d(sm.kv[st][3], &tmv, &sm.full[st], 64, r);
+        const CUtensorMap* tm = (u & 1) ? &tmv : &tmk;
+        mbar_arrive_expect_tx(&sm.full[sl], 2 * kFHalf);
+        tma_load_2d(sm.kv[sl][0], tm, &sm.full[sl], 0, r);
+        tma_load_2d(sm.kv[sl][1], tm, &sm.full[sl], 64, r);
         ++issued;
       }
-      for (int st = 0; st < kFStages && st < issued; ++st) {  // no copy in flight at exit
-        const int last = st + ((issued - 1 - st) / kFStages) * kFStages;
-        mbar_wait(&sm.full[st], (last / kFStages) & 1, err, nullptr);
+      for (int sl = 0; sl < kFSlots && sl < issued; ++sl) {  // no copy in flight at exit
+        const int last = sl + ((issued - 1 - sl) / kFSlots) * kFSlots;
+        mbar_wait(&sm.full[sl], (last / kFSlots) & 1, err, nullptr);
       }
     }
   } else if (warp == kFSoftmaxWarps + 1) {
     // ---------------- MMA issuer ----------------
     // Tensor-pipe order: S_A(0) S_B(0) | PV_A(i) S_A(i+1) PV_B(i) S_B(i+1) | ...
-    // so each group's softmax overlaps the other group's MMAs.
+    // so each group's softmax overlaps the other group's MMAs.  Tile B's
+    // positions follow tile A's, so B uses every key tile A uses (nt_b >= nt_a).
     if (lane == 0) {
       constexpr uint32_t id_s = umma_idesc_m128(kFKeys, false);  // S = Q K^T: both K-major (over dims)
       constexpr uint32_t id_pv = umma_idesc_m128(kFD, true);     // O += P V: V is N(dims)-major
-      const uint32_t pb = smem_u32(sm.p[0]);
+      auto wait_unit = [&](int u) -> bool {
+        if (!mbar_wait(&sm.full[u % kFSlots], (u / kFSlots) & 1, err, abort)) return false;
+        tc_fence_after();
+        return true;
+      };
       auto issue_s = [&](int t, int i) {
-        const uint32_t qb = smem_u32(sm.q[t][0]), kb = smem_u32(sm.kv[i % kFStages][0]);
+        const uint32_t qb = smem_u32(sm.q[t][0]), kb = smem_u32(sm.kv[(2 * i) % kFSlots][0]);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // 16 dims per step
           const uint32_t off = (uint32_t)((kk >> 2) * kFHalf + (kk & 3) * 32);
@@ -184,7 +197,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
       auto issue_pv = [&](int t, int i) -> bool {
         if (!mbar_wait(&sm.p_full[t], i & 1, err, abort)) return false;
         tc_fence_after();
-        const uint32_t vb = smem_u32(sm.kv[i % kFStages][2]);
+        const uint32_t pb = smem_u32(sm.p[t][0]), vb = smem_u32(sm.kv[(2 * i + 1) % kFSlots][0]);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // 16 keys per step
           const uint64_t a = umma_desc_sw128(pb + (uint32_t)((kk >> 2) * kFHalf + (kk & 3) * 32));
@@ -194,24 +207,24 @@ __global__ void __launch_bounds__(kFThreads, 1)
         umma_commit(&sm.pv_done[t]);
         return true;
       };
-      auto wait_full = [&](int i) -> bool {
-        if (!mbar_wait(&sm.full[i % kFStages], (i / kFStages) & 1, err, abort)) return false;
-        tc_fence_after();
-        return true;
-      };
-      bool ok = nkv > 0 && wait_full(0);
+      bool ok = nkv > 0 && wait_unit(0);
       if (ok) {
         if (nt_a > 0) issue_s(0, 0);
         if (have_b) issue_s(1, 0);
+        umma_commit(&sm.empty[0]);  // K_0 consumed
       }
       for (int i = 0; ok && i < nkv; ++i) {
         const bool more = i + 1 < nkv;
+        if (!(ok = wait_unit(2 * i + 1))) break;  // V_i
         if (i < nt_a && !(ok = issue_pv(0, i))) break;
-        if (more && !(ok = wait_full(i + 1))) break;
-        if (i + 1 < nt_a) issue_s(0, i + 1);
+        if (more && !(ok = wait_unit(2 * i + 2))) break;  // K_{i+1}
+        if (more && i + 1 < nt_a) issue_s(0, i + 1);
         if (have_b && i < nt_b && !(ok = issue_pv(1, i))) break;
-        if (have_b && i + 1 < nt_b) issue_s(1, i + 1);
-        umma_commit(&sm.empty[i % kFStages]);  // K_i and V_i consumed
+        umma_commit(&sm.empty[(2 * i + 1) % kFSlots]);  // V_i consumed
+        if (more) {
+          if (have_b && i + 1 < nt_b) issue_s(1, i + 1);
+          umma_commit(&sm.empty[(2 * i + 2) % kFSlots]);  // K_{i+1} consumed
+        }
       }
     }
   } else {
@@ -219,9 +232,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     // Rows past the end of the chunk are never stored and each MMA row is
     // independent, so they need no masking: only tiles that cross the causal
     // diagonal are masked.  The running maximum is kept on raw scores (the
-    // scale is positive), so each exponent is one FFMA + EX2.  The P buffer
-    // is shared: the writes alternate A(0) B(0) A(1) B(1) ..., each after the
-    // previous P.V has finished reading it.
+    // scale is positive), so each exponent is one FFMA + EX2.
     const int t = warp / kFGroupWarps, r = threadIdx.x % 128, p = r % P;
     const int qs = qs0 + t * P, rows_here = t ? rows_b : rows_a, ntiles = t ? nt_b : nt_a;
     const bool row_valid = p < rows_here;
@@ -256,9 +267,12 @@ __global__ void __launch_bounds__(kFThreads, 1)
 #pragma unroll
         for (int u = 0; u < 4; ++u) mx[u] = fmaxf(mx[u], sv[j + u]);
       }
-      const float m_new = fmaxf(m, fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])));
+      // m: the row's reference maximum (raw score); it moves to the tile's
+      // maximum only when that exceeds it by more than 8 / scale_log2.
+      const float m_tile = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      const float m_new = (m_tile - m) * scale_log2 > kFRescaleLog2 ? m_tile : m;  // m = -inf: moves
       const float msc = (m_new == -INFINITY ? 0.f : m_new) * scale_log2;
-      const float alpha = fast_exp2(fmaf(m, scale_log2, -msc));  // m = -inf: 0
+      const float alpha = m_new == m ? 1.f : fast_exp2(fmaf(m, scale_log2, -msc));  // m = -inf: 0
       float rs[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int j = 0; j < kFKeys; j += 4) {
@@ -270,24 +284,10 @@ __global__ void __launch_bounds__(kFThreads, 1)
       }
       l = l * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
       m = m_new;
-      // The P.V issued just before this one (the other tile's at the same
-      // step, or this tile's previous) must be done: it reads the shared P
-      // buffer, and it follows this tile's own previous P.V, which updates O.
-      int wt = -1, wi = 0;
-      if (t == 0 && i > 0) {
-        wt = have_b ? 1 : 0;
-        wi = i - 1;
-      } else if (t == 1) {
-        if (i < nt_a) {
-          wt = 0;
-          wi = i;
-        } else if (i > 0) {
-          wt = 1;
-          wi = i - 1;
-        }
-      }
-      if (wt >= 0) {
-        if (!mbar_wait(&sm.pv_done[wt], wi & 1, err, abort)) {
+      // This tile's previous P.V must be done: it reads this tile's P
+      // buffer and updates O, which a rescale reads below.
+      if (i > 0) {
+        if (!mbar_wait(&sm.pv_done[t], (i - 1) & 1, err, abort)) {
           ok = false;
           break;
         }
@@ -311,7 +311,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
         v.y = pack_bf16(sv[8 * c + 2], sv[8 * c + 3]);
         v.z = pack_bf16(sv[8 * c + 4], sv[8 * c + 5]);
         v.w = pack_bf16(sv[8 * c + 6], sv[8 * c + 7]);
-        *reinterpret_cast<uint4*>(sm.p[c >> 3] + swz128(r, c & 7)) = v;
+        *reinterpret_cast<uint4*>(sm.p[t][c >> 3] + swz128(r, c & 7)) = v;
       }
       fence_proxy_async();
       tc_fence_before();

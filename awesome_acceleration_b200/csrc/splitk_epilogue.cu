@@ -29,7 +29,7 @@ __global__ void __launch_bounds__(128)
   const int64_t N = (int64_t)heads * 128;
   const float* src = part + m * N + (int64_t)hh * 128 + 4 * lane;
   float4 s4 = ld4(src);
-#pragma unroll 4  // several splits' loads in flight; additions stay in split order
+#pragma unroll 8  // several splits' loads in flight; additions stay in split order
   for (int s = 1; s < S; ++s) {
     const float4 b = ld4(src + (int64_t)s * M * N);
     s4.x += b.x;
@@ -60,7 +60,7 @@ __global__ void splitk_silu_kernel(const float* __restrict__ part, int S, int64_
     g[0] = a.x; g[1] = a.y; g[2] = a.z; g[3] = a.w; g[4] = b.x; g[5] = b.y; g[6] = b.z; g[7] = b.w;
     u[0] = c.x; u[1] = c.y; u[2] = c.z; u[3] = c.w; u[4] = d.x; u[5] = d.y; u[6] = d.z; u[7] = d.w;
   }
-#pragma unroll 4
+#pragma unroll 8
   for (int s = 1; s < S; ++s) {
     const float* gs = g0 + (int64_t)s * M * N;
     float4 a = ld4(gs), b = ld4(gs + 4), c = ld4(gs + 64), d = ld4(gs + 68);

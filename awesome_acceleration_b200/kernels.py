@@ -211,6 +211,69 @@ def splitk_reduce(partial, splits: int, out):
     return out
 
 
+# ---------------------------------------------------------------- small-batch decode projections
+SKINNY_MAX_ROWS = 64      # what the kernels take
+SKINNY_DEFAULT_ROWS = 32  # batches the engine sends through them
+SKINNY_FUSED_ROWS = 8     # up to here the QKV / SiLU epilogues run in the GEMM's last split CTAs
+SKINNY_TARGET_CTAS = 296      # QKV / gate-up grids: about two CTAs per SM
+SKINNY_TARGET_CTAS_ROW = 148  # o / down grids: fewer splits for the norm kernel to sum
+
+
+def pick_skinny_splits(M: int, N: int, K: int, target: int = 296, max_elems: int | None = None,
+                       cap: int = 64) -> int:
+    """Split count of the small-batch GEMMs: the largest divisor d <= cap of
+    K/64 with (N/128) * d CTAs at most `target` (two per SM by default: a CTA
+    takes ~74-98 KB of shared memory), fp32 partials no more than half the
+    weight bytes (4 * d * M <= K) and d * M * N fitting `max_elems`; 1 when
+    the weight tiles alone reach the target."""
+    tiles, nk = N // 128, K // 64
+    best = 1
+    for d in range(1, min(nk, cap) + 1):
+        if (nk % d == 0 and tiles * d <= target and 4 * d * M <= K
+                and (max_elems is None or d * M * N <= max_elems)):
+            best = d
+    return best
+
+
+def _check_counters(counters, N: int, what: str):
+    if counters.dtype != torch.int32 or counters.numel() < N // 128:
+        raise ValueError(f"{what}: counters must be int32 with at least {N // 128} entries")
+
+
+def gemm_skinny_splitk(x, w, partial, splits: int):
+    """partial [splits, M, N] fp32 <- split-K partial products of x @ w^T
+    (M <= 64 rows; the weights are the MMA's 128-row operand)."""
+    M, K = x.shape
+    N = w.shape[0]
+    _lib.check(_lib_().aacc_gemm_skinny_splitk(_p(x), _p(w), _p(partial), M, N, K, splits, _stream()),
+               "gemm_skinny_splitk")
+    return partial
+
+
+def skinny_qkv_norm_rope_store(x, w_qkv, partial, splits: int, counters, q_norm_w, k_norm_w, eps: float, positions,
+                               rope_cos_sin, slot_mapping, k_cache, v_cache, num_q_heads: int, q_out):
+    """QKV projection + q/k norm + RoPE + KV store for M <= 64 rows in one
+    launch (the epilogue runs in the last split CTA of each head)."""
+    M, K = x.shape
+    nb, hkv, bs, _ = k_cache.shape
+    _check_counters(counters, w_qkv.shape[0], "skinny_qkv_norm_rope_store")
+    _lib.check(_lib_().aacc_skinny_qkv_norm_rope_store(
+        _p(x), _p(w_qkv), _p(partial), splits, _p(counters), _p(q_norm_w), _p(k_norm_w), eps, _p(positions),
+        _p(rope_cos_sin), rope_cos_sin.shape[0], _p(slot_mapping), _p(q_out), _p(k_cache), _p(v_cache), nb,
+        num_q_heads, hkv, bs, M, K, _stream()), "skinny_qkv_norm_rope_store")
+    return q_out
+
+
+def skinny_silu_mul(x, w_gate_up, partial, splits: int, counters, out):
+    """out [M, I] = SiLU(gate) * up for M <= 64 rows in one launch."""
+    M, K = x.shape
+    I = w_gate_up.shape[0] // 2
+    _check_counters(counters, 2 * I, "skinny_silu_mul")
+    _lib.check(_lib_().aacc_skinny_silu_mul(_p(x), _p(w_gate_up), _p(partial), splits, _p(counters), _p(out), M, I, K,
+                                            _stream()), "skinny_silu_mul")
+    return out
+
+
 def gemm_silu_mul(x, w_gate_up, out=None):
     M, K = x.shape
     I = w_gate_up.shape[0] // 2

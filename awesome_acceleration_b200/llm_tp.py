@@ -342,6 +342,8 @@ class LLMTP:
         """Send one decode step to the workers, stage it if the batch changed, run it
         here and queue the read-back of its tokens."""
         B = len(slots)
+        if B > rt.max_batch:  # before the workers are sent into this step's collectives
+            raise ValueError(f"decode batch {B} exceeds the runtime's max_batch {rt.max_batch}")
         self._send({"action": "decode", "batch_size": B, "restage": restage, "slots": slots if restage else None})
         if restage:
             self._stage_decode([active[s][2][-1] for s in slots], [active[s][3] for s in slots], slots,

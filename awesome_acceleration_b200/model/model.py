@@ -196,7 +196,7 @@ class Qwen3ForCausalLM(nn.Module):
         cfg = self.config
         self.kv = PagedKVCache(cfg.num_hidden_layers, cfg.num_key_value_heads, num_slots, max_seq_len,
                                block_size=block_size, num_blocks=num_blocks, device=device, dtype=dtype)
-        self.max_batch = max_batch or min(num_slots, 256) or 1
+        self.max_batch = max_batch or num_slots or 1  # a decode step may hold every slot
         for i, layer in enumerate(self.model.layers):
             attn = layer.self_attn
             attn._kv_cache = self.kv.k[i]

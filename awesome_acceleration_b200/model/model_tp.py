@@ -147,7 +147,7 @@ class Qwen3ForCausalLMTP(nn.Module):
         cfg = self.config
         self.kv = PagedKVCache(cfg.num_hidden_layers, cfg.num_key_value_heads // self.tp_size, num_slots,
                                max_seq_len, block_size=block_size, num_blocks=num_blocks, device=device, dtype=dtype)
-        self.max_batch = max_batch or min(num_slots, 256) or 1
+        self.max_batch = max_batch or num_slots or 1  # a decode step may hold every slot
         for i, layer in enumerate(self.model.layers):
             attn = layer.self_attn
             attn._kv_cache, attn._v_cache, attn._cache_seqlens = self.kv.k[i], self.kv.v[i], self.kv.seqlens

@@ -194,6 +194,8 @@ class _DecodeBuffers:
         # split-K fp32 partials of the decode projections (the split count is
         # capped so that splits * B * N fits): 32 MB
         self.part = torch.empty(max(8 << 20, 16 * B * H), dtype=torch.float32, device=device)
+        # per-128-row-tile arrival counters of the small-batch GEMMs (zero between launches)
+        self.sk_cnt = torch.zeros(4096, dtype=torch.int32, device=device)
         if tp > 1:  # this rank's argmax candidates (ids | fp32 scores) and the all-gathered [tp, 2 B]
             self.cand = torch.zeros(2 * B, **i64)
             self.g_cand = torch.zeros(tp * 2 * B, **i64)
@@ -220,6 +222,7 @@ class Qwen3Runtime:
         self.use_graphs = use_graphs
         self.chunk = prefill_chunk_tokens
         self.cluster_gemm = os.environ.get("AACC_CLUSTER_GEMM", "0") == "1"
+        self.skinny_rows = int(os.environ.get("AACC_SKINNY_ROWS", str(K.SKINNY_DEFAULT_ROWS)))
         self.device = embed.device
         self.max_context = kv.max_blocks * kv.block_size
         self.buf = _DecodeBuffers(max_batch, hidden, self.Hq, self.I, self.vocab_local, tp, self.max_context,
@@ -258,10 +261,35 @@ class Qwen3Runtime:
         remote reduction cost as much latency as the launch they remove."""
         return part is not None and 0 < M <= K.CLUSTER_MAX_ROWS and self.cluster_gemm
 
+    def _skinny(self, M, part) -> bool:
+        """Decode batches of at most `skinny_rows` rows (AACC_SKINNY_ROWS)
+        run the small-batch GEMMs: weights as the MMA's 128-row operand, a
+        third of the shared memory per CTA, so two or three CTAs share an SM
+        and a projection's weight stream overlaps the kernel before it; up to
+        SKINNY_FUSED_ROWS rows the QKV / SiLU epilogues finish in the same
+        launch (beyond that the tile's last CTA would walk too many rows, and
+        the epilogue kernels run them in parallel)."""
+        return part is not None and 0 < M <= min(self.skinny_rows, K.SKINNY_MAX_ROWS) and not self.cluster_gemm
+
+    def _skinny_part(self, M, w, part, target):
+        N, Kd = w.shape
+        sp = K.pick_skinny_splits(M, N, Kd, target=target, max_elems=part.numel())
+        return sp, part[:sp * M * N].view(sp, M, N)
+
     def _qkv(self, i, lw, x, positions, slot_map, q, part):
         """Fused QKV projection + q/k-norm + RoPE + KV store (model/model.py:219-226)."""
         kv = self.kv
         M = x.shape[0]
+        if self._skinny(M, part):
+            sp, pv = self._skinny_part(M, lw.wqkv, part, K.SKINNY_TARGET_CTAS)
+            if M <= K.SKINNY_FUSED_ROWS:
+                K.skinny_qkv_norm_rope_store(x, lw.wqkv, pv, sp, self.buf.sk_cnt, lw.q_norm, lw.k_norm, self.eps,
+                                             positions, self.rope, slot_map, kv.k[i], kv.v[i], self.Hq, q_out=q)
+            else:
+                K.gemm_skinny_splitk(x, lw.wqkv, pv, sp)
+                K.splitk_qkv_norm_rope_store(pv, sp, lw.q_norm, lw.k_norm, self.eps, positions, self.rope, slot_map,
+                                             kv.k[i], kv.v[i], self.Hq, q_out=q)
+            return
         if self._cluster(M, part):
             K.qkv_norm_rope_store_cluster(x, lw.wqkv, lw.q_norm, lw.k_norm, self.eps, positions, self.rope, slot_map,
                                           kv.k[i], kv.v[i], self.Hq, q_out=q)
@@ -280,6 +308,14 @@ class Qwen3Runtime:
     def _gate_up(self, lw, x, act, part):
         """gate/up projection + SiLU-mul (model/model.py:189-190)."""
         M = x.shape[0]
+        if self._skinny(M, part):
+            sp, pv = self._skinny_part(M, lw.w_gate_up, part, K.SKINNY_TARGET_CTAS)
+            if M <= K.SKINNY_FUSED_ROWS:
+                K.skinny_silu_mul(x, lw.w_gate_up, pv, sp, self.buf.sk_cnt, act)
+            else:
+                K.gemm_skinny_splitk(x, lw.w_gate_up, pv, sp)
+                K.splitk_silu_mul(pv, sp, act)
+            return
         if self._cluster(M, part):
             K.gemm_silu_mul_cluster(x, lw.w_gate_up, out=act)
             return
@@ -309,10 +345,15 @@ class Qwen3Runtime:
             self.comm.all_reduce(delta)
             K.add_rmsnorm(delta, res, norm_w, self.eps, out=x)
             return
-        splits = self._splits(M, w, part)
-        if splits > 1:
-            pv = part[:splits * M * w.shape[0]].view(splits, M, w.shape[0])
-            K.gemm_splitk(inp, w, pv, splits)
+        if self._skinny(M, part):
+            splits, pv = self._skinny_part(M, w, part, K.SKINNY_TARGET_CTAS_ROW)
+            K.gemm_skinny_splitk(inp, w, pv, splits)
+        else:
+            splits = self._splits(M, w, part)
+            pv = part[:splits * M * w.shape[0]].view(splits, M, w.shape[0]) if splits > 1 else None
+            if splits > 1:
+                K.gemm_splitk(inp, w, pv, splits)
+        if pv is not None:
             if self.comm.size == 1:
                 K.splitk_add_rmsnorm(pv, splits, res, norm_w, self.eps, out=x)
                 return

@@ -376,6 +376,22 @@ def run_attn(args, device):
             e1.synchronize()
             times.append(e0.elapsed_time(e1) / 1e3)
     _lib.raise_on_device_error("attn bench")
+    # spot-check: a few output rows against a plain torch fp32 attention over
+    # the same paged K/V (the kernel rounds P to bf16 before P.V)
+    G = hq // hkv
+    check_err = 0.0
+    for b in sorted({0, 1, B // 2, B - 1}):
+        n = ctx[b]
+        blocks = bt[b, :(n + bs - 1) // bs].long().to(device)
+        kk = kc[blocks].permute(1, 0, 2, 3).reshape(hkv, -1, 128)[:, :n].float()
+        vv = vc[blocks].permute(1, 0, 2, 3).reshape(hkv, -1, 128)[:, :n].float()
+        qq = q[b].float().view(hkv, G, 128)
+        p = torch.softmax(qq @ kk.transpose(1, 2) * 128 ** -0.5, dim=-1)
+        ref = (p @ vv).reshape(hq, 128)
+        check_err = max(check_err, (out[b].float() - ref).abs().max().item())
+    check_tol = 2e-2
+    if not check_err <= check_tol:
+        raise RuntimeError(f"attn bench: output rows differ from torch fp32 attention by {check_err:.3g}")
     t = statistics.mean(times)
     byts = attention_bytes(ctx, hq, hkv, bs)
     pk, kind = peaks()
@@ -385,7 +401,9 @@ def run_attn(args, device):
             "ms_per_step": round(t * 1e3, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "cfg3 decode-attention microbenchmark", "pool_blocks": nb,
-                       "l2": "flushed between launches"},
+                       "l2": "flushed between launches",
+                       "output_check": {"rows": 4, "vs": "torch fp32 attention", "max_abs_err": round(check_err, 5),
+                                        "tol": check_tol}},
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(ach / pk["hbm_gbs"], 3), "traffic": int(byts * ATTN_TRAFFIC_PER_ALG_BYTE),
                          "traffic_source": ATTN_TRAFFIC_SOURCE, "peak_kind": kind},
@@ -713,19 +731,29 @@ def run_cfg5(args, device):
 
 # --------------------------------------------------------------------------- prefill GEMMs (tensor pipe)
 def run_decode_projections(args, device):
-    """The decode projections of one layer as the engine runs them at B rows
-    (cfg2: Qwen3-0.6B, B = 256): QKV + q/k-norm + RoPE + KV store, o_proj +
-    residual add + RMSNorm, gate/up + SiLU, down + residual add + RMSNorm, over
-    28 layers of distinct weights (840 MB, so every layer streams its weights
-    from HBM), captured in one CUDA graph per variant:
-      * cluster: cluster split-K kernels (partials in distributed shared memory,
-        epilogues fused) + add_rmsnorm;
-      * splitk: split-K partials through HBM + epilogue kernels.
-    Reports us per layer for the whole sequence and for each projection alone."""
+    """The decode projections of one layer as the engine runs them at B rows:
+    QKV + q/k-norm + RoPE + KV store, o_proj + residual add + RMSNorm,
+    gate/up + SiLU, down + residual add + RMSNorm, over layers of distinct
+    weights (Qwen3-0.6B shapes: 28 layers, 840 MB; --proj-shapes 8b: Qwen3-8B
+    shapes, 8 layers, 3.1 GB; larger than L2 either way, so every layer streams
+    its weights from HBM), captured in one CUDA graph per variant:
+      * splitk: split-K partials through L2 + epilogue kernels (B > 32);
+      * skinny_fused: small-batch GEMMs (weights as the 128-row MMA operand),
+        QKV / SiLU epilogues in the same launch (the engine's path up to
+        SKINNY_FUSED_ROWS rows); skinny: the same GEMMs with the split-K
+        epilogue kernels (the engine's path up to SKINNY_DEFAULT_ROWS); o / down
+        partials summed by the norm kernel in both (B <= 64);
+      * cluster: cluster split-K kernels (partials in distributed shared
+        memory, epilogues fused) + add_rmsnorm (opt-in in the engine).
+    Reports us per layer for the whole sequence and for each projection
+    alone; `value` and the roofline are the engine's default path at B."""
     from awesome_acceleration_b200 import _lib, kernels as Kk
     from awesome_acceleration_b200.runtime import interleave_gate_up, rope_table
     B = args.batch or (32 if args.small else 256)
-    L, H, I, hq, hkv, bs = 28, 1024, 3072, 16, 8, 256
+    if args.proj_shapes == "8b":
+        L, H, I, hq, hkv, bs, model = 8, 4096, 12288, 32, 8, 256, "Qwen3-8B"
+    else:
+        L, H, I, hq, hkv, bs, model = 28, 1024, 3072, 16, 8, 256, "Qwen3-0.6B"
     g = torch.Generator(device=device).manual_seed(3)
 
     def rnd(*shape, std=0.02):
@@ -738,7 +766,7 @@ def run_decode_projections(args, device):
                        "qn": torch.ones(128, dtype=torch.bfloat16, device=device),
                        "kn": torch.ones(128, dtype=torch.bfloat16, device=device),
                        "ln": torch.ones(H, dtype=torch.bfloat16, device=device)})
-    layers = layers * (L // len(layers))  # --hot-weights: one layer's weights 28 times (L2-resident)
+    layers = layers * (L // len(layers))  # --hot-weights: one layer's weights L times (L2-resident)
     x, res = rnd(B, H, std=1.0), rnd(B, H, std=1.0)
     attn, act, delta = rnd(B, hq * 128, std=1.0), rnd(B, I, std=1.0), rnd(B, H)
     q = torch.empty((B, hq, 128), dtype=torch.bfloat16, device=device)
@@ -749,16 +777,30 @@ def run_decode_projections(args, device):
     vc = torch.zeros_like(kc)
     slots = torch.randperm(nb * bs, device=device)[:B]
     part = torch.empty(max(8 << 20, 16 * B * H), dtype=torch.float32, device=device)
+    cnt = torch.zeros(4096, dtype=torch.int32, device=device)
 
     def pv(M, N, splits):
         return part[:splits * M * N].view(splits, M, N)
 
-    def qkv(lw, cluster):
-        if cluster:
+    def sk_splits(N, Kd, target):
+        return Kk.pick_skinny_splits(B, N, Kd, target=target, max_elems=part.numel())
+
+    def qkv(lw, variant):
+        N = lw["qkv"].shape[0]
+        if variant == "cluster":
             Kk.qkv_norm_rope_store_cluster(x, lw["qkv"], lw["qn"], lw["kn"], 1e-6, pos, rope, slots, kc, vc, hq,
                                            q_out=q)
             return
-        N = lw["qkv"].shape[0]
+        if variant == "skinny_fused":
+            sp = sk_splits(N, H, Kk.SKINNY_TARGET_CTAS)
+            Kk.skinny_qkv_norm_rope_store(x, lw["qkv"], pv(B, N, sp), sp, cnt, lw["qn"], lw["kn"], 1e-6, pos, rope,
+                                          slots, kc, vc, hq, q)
+            return
+        if variant == "skinny":
+            sp = sk_splits(N, H, Kk.SKINNY_TARGET_CTAS)
+            Kk.gemm_skinny_splitk(x, lw["qkv"], pv(B, N, sp), sp)
+            Kk.splitk_qkv_norm_rope_store(pv(B, N, sp), sp, lw["qn"], lw["kn"], 1e-6, pos, rope, slots, kc, vc, hq, q)
+            return
         sp = Kk.pick_splits(B, N, H, max_elems=part.numel())
         if sp > 1:
             Kk.gemm_splitk(x, lw["qkv"], pv(B, N, sp), sp)
@@ -766,12 +808,17 @@ def run_decode_projections(args, device):
         else:
             Kk.qkv_norm_rope_store(x, lw["qkv"], lw["qn"], lw["kn"], 1e-6, pos, rope, slots, kc, vc, hq, q_out=q)
 
-    def row(inp, wt, ln, cluster):
-        if cluster:
+    def row(inp, wt, ln, variant):
+        N, Kd = wt.shape
+        if variant == "cluster":
             Kk.gemm_cluster(inp, wt, out=delta)
             Kk.add_rmsnorm(delta, res, ln, 1e-6, out=x)
             return
-        N, Kd = wt.shape
+        if variant.startswith("skinny"):
+            sp = sk_splits(N, Kd, Kk.SKINNY_TARGET_CTAS_ROW)
+            Kk.gemm_skinny_splitk(inp, wt, pv(B, N, sp), sp)
+            Kk.splitk_add_rmsnorm(pv(B, N, sp), sp, res, ln, 1e-6, out=x)
+            return
         sp = Kk.pick_splits(B, N, Kd, max_elems=part.numel())
         if sp > 1:
             Kk.gemm_splitk(inp, wt, pv(B, N, sp), sp)
@@ -780,9 +827,18 @@ def run_decode_projections(args, device):
             Kk.gemm(inp, wt, out=delta)
             Kk.add_rmsnorm(delta, res, ln, 1e-6, out=x)
 
-    def gate_up(lw, cluster):
-        if cluster:
+    def gate_up(lw, variant):
+        if variant == "cluster":
             Kk.gemm_silu_mul_cluster(x, lw["gu"], out=act)
+            return
+        if variant == "skinny_fused":
+            sp = sk_splits(2 * I, H, Kk.SKINNY_TARGET_CTAS)
+            Kk.skinny_silu_mul(x, lw["gu"], pv(B, 2 * I, sp), sp, cnt, act)
+            return
+        if variant == "skinny":
+            sp = sk_splits(2 * I, H, Kk.SKINNY_TARGET_CTAS)
+            Kk.gemm_skinny_splitk(x, lw["gu"], pv(B, 2 * I, sp), sp)
+            Kk.splitk_silu_mul(pv(B, 2 * I, sp), sp, act)
             return
         sp = Kk.pick_splits(B, 2 * I, H, max_elems=part.numel())
         if sp > 1:
@@ -791,20 +847,22 @@ def run_decode_projections(args, device):
         else:
             Kk.gemm_silu_mul(x, lw["gu"], out=act)
 
-    ops = {"qkv": lambda lw, c: qkv(lw, c), "o_norm": lambda lw, c: row(attn, lw["o"], lw["ln"], c),
-           "gate_up": lambda lw, c: gate_up(lw, c), "down_norm": lambda lw, c: row(act, lw["d"], lw["ln"], c)}
+    ops = {"qkv": lambda lw, v: qkv(lw, v), "o_norm": lambda lw, v: row(attn, lw["o"], lw["ln"], v),
+           "gate_up": lambda lw, v: gate_up(lw, v), "down_norm": lambda lw, v: row(act, lw["d"], lw["ln"], v)}
     seqs = {"layer": list(ops)} | {k: [k] for k in ops}
+    variants = (["skinny_fused", "skinny"] if B <= Kk.SKINNY_MAX_ROWS else []) + ["splitk"] + (
+        [] if args.no_cluster else ["cluster"])
+    engine = ("skinny_fused" if B <= Kk.SKINNY_FUSED_ROWS else "skinny") if B <= Kk.SKINNY_DEFAULT_ROWS else "splitk"
     stream = torch.cuda.current_stream()
     res_us = {}
     pk, kind = peaks()
     with ClockSampler(torch.cuda.current_device()) as clk:
-        for variant in ("cluster", "splitk"):
-            cl = variant == "cluster"
+        for variant in variants:
             for name, seq in seqs.items():
                 def body():
                     for lw in layers:
                         for op in seq:
-                            ops[op](lw, cl)
+                            ops[op](lw, variant)
                 body()  # eager warm-up (plans, tensor maps, smem attributes)
                 torch.cuda.synchronize()
                 graph = torch.cuda.CUDAGraph()
@@ -829,17 +887,29 @@ def run_decode_projections(args, device):
     _lib.raise_on_device_error("decode projections")
     w_layer = 2 * ((hq + 2 * hkv) * 128 * H + H * hq * 128 + 2 * I * H + H * I)
     flops = 2 * B * w_layer / 2
-    t = res_us["cluster.layer"] * 1e-6
-    plans = {"qkv": Kk.gemm_cluster_plan(B, (hq + 2 * hkv) * 128, H), "o": Kk.gemm_cluster_plan(B, H, hq * 128),
-             "gate_up": Kk.gemm_cluster_plan(B, 2 * I, H), "down": Kk.gemm_cluster_plan(B, H, I)}
-    return {"metric": f"decode projections us per layer (Qwen3-0.6B shapes, B={B})", "value": res_us["cluster.layer"],
+    t = res_us[f"{engine}.layer"] * 1e-6
+    by_variant = {v: {"us_per_layer": res_us[f"{v}.layer"],
+                      "weight_GBps": round(w_layer / (res_us[f"{v}.layer"] * 1e-6) / 1e9, 1),
+                      "frac_of_hbm": round(w_layer / (res_us[f"{v}.layer"] * 1e-6) / 1e9 / pk["hbm_gbs"], 3)}
+                  for v in variants}
+    cfg = {"workload": f"decode projections of one layer ({model} shapes), " + (
+               f"one layer's weights {L} times (L2-resident)" if args.hot_weights
+               else f"{L} layers of distinct weights per graph"),
+           "engine_path": engine, "per_variant_us": res_us, "per_variant": by_variant,
+           "weight_bytes_per_layer": w_layer, "l2": f"weights {L * w_layer / 1e6:.0f} MB > L2"}
+    if "skinny" in variants:
+        cfg["skinny_rows"] = {"engine_up_to": Kk.SKINNY_DEFAULT_ROWS, "fused_epilogues_up_to": Kk.SKINNY_FUSED_ROWS}
+        cfg["skinny_splits"] = {"qkv": sk_splits((hq + 2 * hkv) * 128, H, Kk.SKINNY_TARGET_CTAS),
+                                "o": sk_splits(H, hq * 128, Kk.SKINNY_TARGET_CTAS_ROW),
+                                "gate_up": sk_splits(2 * I, H, Kk.SKINNY_TARGET_CTAS),
+                                "down": sk_splits(H, I, Kk.SKINNY_TARGET_CTAS_ROW)}
+    if "cluster" in variants:
+        cfg["cluster_plans (mt, m_tiles, splits)"] = {
+            "qkv": Kk.gemm_cluster_plan(B, (hq + 2 * hkv) * 128, H), "o": Kk.gemm_cluster_plan(B, H, hq * 128),
+            "gate_up": Kk.gemm_cluster_plan(B, 2 * I, H), "down": Kk.gemm_cluster_plan(B, H, I)}
+    return {"metric": f"decode projections us per layer ({model} shapes, B={B})", "value": res_us[f"{engine}.layer"],
             "unit": "us per layer", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "decode projections of one layer, " + (
-                           "one layer's weights 28 times (L2-resident)" if args.hot_weights
-                           else "28 layers of distinct weights per graph"),
-                       "per_variant_us": res_us, "cluster_plans (mt, m_tiles, splits)": plans,
-                       "l2": "weights 840 MB > L2"},
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": cfg,
             "roofline": {"bound": "hbm", "achieved": round(w_layer / t / 1e9, 1), "peak": pk["hbm_gbs"],
                          "unit": "GB/s", "frac": round(w_layer / t / 1e9 / pk["hbm_gbs"], 3), "traffic": None,
                          "peak_kind": kind, "tensor_tflops": round(flops / t / 1e12, 1)},
@@ -992,6 +1062,13 @@ def main():
                     help="cfg2: skip the cfg4 (Qwen3-8B) tensor-parallel block at TP = the world")
     ap.add_argument("--decode", action="store_true", help="gemm workload: decode-batch shapes")
     ap.add_argument("--batch", type=int, default=0, help="gemm --decode: batch rows (default 256)")
+    ap.add_argument("--proj-shapes", default="0.6b", choices=["0.6b", "8b"],
+                    help="gemm --decode: Qwen3-0.6B (28 layers) or Qwen3-8B (8 layers) projection shapes")
+    ap.add_argument("--no-cluster", action="store_true", help="gemm --decode: skip the cluster variant")
+    ap.add_argument("--skinny-ctas", type=int, default=0,
+                    help="target CTAs of the small-batch QKV / gate-up grids (default: the library's)")
+    ap.add_argument("--skinny-ctas-row", type=int, default=0,
+                    help="target CTAs of the small-batch o / down grids (default: the library's)")
     ap.add_argument("--hot-weights", action="store_true",
                     help="gemm --decode: reuse one layer's weights (L2-resident) to bound what prefetching could gain")
     ap.add_argument("--midrun", action="store_true",
@@ -999,6 +1076,10 @@ def main():
     ap.add_argument("--profile", action="store_true",
                     help="profiler capture: warm-up + timed jobs only (no roofline/e2e/CPU legs)")
     args = ap.parse_args()
+    if args.skinny_ctas or args.skinny_ctas_row:
+        from awesome_acceleration_b200 import kernels as _k
+        _k.SKINNY_TARGET_CTAS = args.skinny_ctas or _k.SKINNY_TARGET_CTAS
+        _k.SKINNY_TARGET_CTAS_ROW = args.skinny_ctas_row or _k.SKINNY_TARGET_CTAS_ROW
     args.world = int(os.environ.get("WORLD_SIZE", "1"))
     args.rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -231,6 +231,39 @@ int aacc_gemm_cluster_plan(int64_t M, int64_t N, int64_t K, int* mt, int* m_tile
  * that fit on the current device at once (0 when none). */
 int64_t aacc_gemm_cluster_capacity(int tile_rows_128, int splits);
 
+/* ---- decode projections of small batches: weights as the 128-row operand -
+ * For 1 <= M <= 64 rows; N % 128 == 0, K % 64 == 0, `splits` divides K / 64.
+ * Each CTA holds four 16 KB weight slabs plus the matching slabs of x, so
+ * two or three CTAs share an SM and a projection streams its weights while
+ * the kernel before it is still running.  The fp32 partials go to
+ * partial[splits][M][N] (as aacc_gemm_splitk).  The _qkv / _silu forms also
+ * finish each 128-row weight tile in the same launch: the tile's last CTA
+ * sums the partials in split order and applies the epilogue of
+ * aacc_splitk_qkv_norm_rope_store / aacc_splitk_silu_mul (same rounding).
+ * `counters` is caller-owned, one int per 128-row tile, zero before the
+ * first call; each launch leaves it zero again unless it reported an error
+ * (then zero it before the next call).  Launches sharing `counters` must be
+ * ordered on one stream. */
+
+/* partial[s][M][N] = x[:, Ks] @ w[:, Ks]^T: o_proj / down_proj of a decode
+ * step (model/model.py:237-238, :189-190), summed by aacc_splitk_add_rmsnorm
+ * or the tensor-parallel exchange. */
+int aacc_gemm_skinny_splitk(const void* x, const void* w, float* partial, int64_t M, int64_t N, int64_t K,
+                            int splits, cudaStream_t stream);
+
+/* QKV projection + q/k RMSNorm + RoPE + paged KV store of a decode step
+ * (model/model.py:219-226, :233-240), as aacc_qkv_norm_rope_store. */
+int aacc_skinny_qkv_norm_rope_store(const void* x, const void* w_qkv, float* partial, int splits, int* counters,
+                                    const void* q_norm_w, const void* k_norm_w, float eps, const int64_t* positions,
+                                    const void* rope_cos_sin, int64_t max_pos, const int64_t* slot_mapping,
+                                    void* q_out, void* k_cache, void* v_cache, int64_t num_blocks, int num_q_heads,
+                                    int num_kv_heads, int block_size, int64_t M, int64_t K, cudaStream_t stream);
+
+/* out[M][I] = bf16(silu(bf16(gate))) * bf16(up) over gate/up rows
+ * interleaved by 64 (model/model.py:189-190), as aacc_gemm_silu_mul. */
+int aacc_skinny_silu_mul(const void* x, const void* w_gate_up, float* partial, int splits, int* counters, void* out,
+                         int64_t M, int64_t I, int64_t K, cudaStream_t stream);
+
 /* out[M][N] = bf16(x[M][K] @ w[N][K]^T + bias[N]): the bias added in fp32
  * before the rounding, as a fused-bias F.linear does.  Column-parallel and
  * QKV-parallel layers built with bias=True (model/parallel_layers.py:72-89,

@@ -19,6 +19,29 @@ def test_pick_splits_invariants_and_cfg2_choices():
                                                                     (1024, 3072))] == [2, 1, 4, 6]
 
 
+def test_pick_skinny_splits_invariants():
+    """Small-batch GEMM split counts: a divisor of K/64 (at most 64, which the
+    tensor-parallel exchange takes), at most `target` CTAs unless the weight
+    tiles alone exceed it, fp32 partials at most half the weight bytes."""
+    from awesome_acceleration_b200.kernels import pick_skinny_splits
+    shapes = ((4096, 1024), (6144, 1024), (1024, 2048), (1024, 3072), (6144, 4096), (24576, 4096), (4096, 12288),
+              (512, 512), (1536, 4096))
+    for M in (1, 8, 16, 32, 64):
+        for N, K in shapes:
+            for target in (148, 296, 444):
+                d = pick_skinny_splits(M, N, K, target=target, max_elems=8 << 20)
+                tiles = N // 128
+                assert (K // 64) % d == 0 and 1 <= d <= 64
+                assert d == 1 or (tiles * d <= target and 4 * d * M <= K and d * M * N <= 8 << 20)
+                # the largest such divisor
+                bigger = [e for e in range(d + 1, min(K // 64, 64) + 1) if (K // 64) % e == 0 and
+                          tiles * e <= target and 4 * e * M <= K and e * M * N <= 8 << 20]
+                assert not bigger, (M, N, K, target, d, bigger)
+    # Qwen3-0.6B decode at one row, two CTAs per SM: QKV 8, gate/up 4, o 32, down 24
+    assert [pick_skinny_splits(1, n, k) for n, k in ((4096, 1024), (6144, 1024), (1024, 2048), (1024, 3072))] == \
+        [8, 4, 32, 24]
+
+
 class _Rt:
     padded_batch = Qwen3Runtime.padded_batch
 

@@ -585,3 +585,113 @@ def test_cluster_gemms_equal_splitk_path(cuda, M):
     caps = {(mt, s): K().gemm_cluster_capacity(mt, s) for mt in (1, 2) for s in (1, 2, 3, 4, 6, 8, 16)}
     print(f"M={M}: plans qkv {K().gemm_cluster_plan(M, 4096, H)}, gate/up {K().gemm_cluster_plan(M, 2 * I, H)}, "
           f"o {K().gemm_cluster_plan(M, H, 2048)}, down {plan}; resident CTAs per (tile rows/128, splits) {caps}")
+
+
+@pytest.mark.parametrize("M", [1, 5, 16, 17, 33, 64])
+def test_skinny_gemms(cuda, M):
+    """Small-batch GEMMs (weights as the MMA's 128-row operand): the split-K
+    partials agree with the general split-K kernel's and sum to torch's fp32
+    product; the fused QKV (norm + RoPE + KV store) and SiLU forms equal
+    gemm_skinny_splitk + the split-K epilogue kernels bit for bit (same
+    partials, same epilogue arithmetic), launch after launch; the arrival
+    counters are zero after every launch."""
+    from awesome_acceleration_b200.runtime import interleave_gate_up, rope_table
+    g = torch.Generator().manual_seed(1000 + M)
+    H, I, hq, hkv, bs = 1024, 3072, 16, 8, 256
+    x = torch.randn((M, H), generator=g).to(BF).to(cuda)
+    a = torch.randn((M, I), generator=g).to(BF).to(cuda)
+    w = {n: (torch.randn(sh, generator=g) * 0.02).to(BF).to(cuda) for n, sh in
+         [("qkv", ((hq + 2 * hkv) * 128, H)), ("d", (H, I)), ("g", (I, H)), ("u", (I, H))]}
+    wgu = interleave_gate_up(w["g"], w["u"]).contiguous()
+    qn = (1 + 0.1 * torch.randn(128, generator=g)).to(BF).to(cuda)
+    kn = (1 + 0.1 * torch.randn(128, generator=g)).to(BF).to(cuda)
+    rope = rope_table(4096, 128, 1e6, cuda)
+    pos = torch.randint(0, 4096, (M,), generator=g).to(cuda)
+    nb = (M + bs - 1) // bs + 2
+    slots = torch.randperm(nb * bs, generator=g)[:M].to(cuda)
+    part = torch.empty(48 * M * 6144, dtype=torch.float32, device=cuda)
+    part2 = torch.empty_like(part)
+    cnt = torch.zeros(1024, dtype=torch.int32, device=cuda)
+    clear_err()
+    exact = {}
+    for wt, inp in ((w["d"], a), (w["qkv"], x), (wgu, x)):
+        N, Kd = wt.shape
+        ref = inp.float() @ wt.float().t()
+        for splits in sorted({1, 2, 4, K().pick_skinny_splits(M, N, Kd)}):
+            if (Kd // 64) % splits:
+                continue
+            pv = part[:splits * M * N].view(splits, M, N)
+            K().gemm_skinny_splitk(inp, wt, pv, splits)
+            pg = part2[:splits * M * N].view(splits, M, N)
+            K().gemm_splitk(inp, wt, pg, splits)
+            torch.cuda.synchronize()
+            d = (pv - pg).abs().max().item()
+            exact[(N, splits)] = d == 0
+            assert d <= 1e-5 * pg.abs().max().item() + 1e-6, (N, splits, d)
+            err = (pv.sum(0) - ref).abs().max().item()
+            assert err <= 1e-3 * ref.abs().max().item() + 1e-4, (N, splits, err)
+    # fused epilogues against the separate epilogue kernels on the same partials
+    N = w["qkv"].shape[0]
+    for splits in sorted({1, 4, K().pick_skinny_splits(M, N, H)}):
+        pv = part[:splits * M * N].view(splits, M, N)
+        outs = []
+        for fused in (False, True, True):  # the second fused launch reuses the counters
+            kc = torch.zeros((nb, hkv, bs, 128), dtype=BF, device=cuda)
+            vc = torch.zeros_like(kc)
+            q = torch.zeros((M, hq, 128), dtype=BF, device=cuda)
+            if fused:
+                K().skinny_qkv_norm_rope_store(x, w["qkv"], pv, splits, cnt, qn, kn, 1e-6, pos, rope, slots, kc, vc,
+                                               hq, q_out=q)
+            else:
+                K().gemm_skinny_splitk(x, w["qkv"], pv, splits)
+                K().splitk_qkv_norm_rope_store(pv, splits, qn, kn, 1e-6, pos, rope, slots, kc, vc, hq, q)
+            outs.append((q, kc, vc))
+        for o in outs[1:]:
+            for t0, t1 in zip(outs[0], o):
+                assert torch.equal(t0, t1), f"qkv M={M} splits={splits}"
+        torch.cuda.synchronize()
+        assert int(cnt.abs().sum().item()) == 0
+    N = 2 * I
+    for splits in sorted({1, 4, K().pick_skinny_splits(M, N, H)}):
+        pv = part[:splits * M * N].view(splits, M, N)
+        K().gemm_skinny_splitk(x, wgu, pv, splits)
+        ref = torch.empty((M, I), dtype=BF, device=cuda)
+        K().splitk_silu_mul(pv, splits, ref)
+        for _ in range(2):
+            out = torch.full((M, I), float("nan"), dtype=BF, device=cuda)
+            K().skinny_silu_mul(x, wgu, pv, splits, cnt, out)
+            assert torch.equal(out, ref), f"silu M={M} splits={splits}"
+        torch.cuda.synchronize()
+        assert int(cnt.abs().sum().item()) == 0
+    assert dev_err() == 0
+    print(f"M={M}: skinny partials bit-equal to the general split-K kernel's: {exact}")
+
+
+def test_skinny_gemm_rejects_bad_shapes(cuda):
+    """Shapes the small-batch kernels do not take are refused before launch."""
+    x = torch.zeros((65, 1024), dtype=BF, device=cuda)
+    w = torch.zeros((1024, 1024), dtype=BF, device=cuda)
+    part = torch.zeros(65 * 1024 * 16, dtype=torch.float32, device=cuda)
+    with pytest.raises(RuntimeError):
+        K().gemm_skinny_splitk(x, w, part, 1)  # 65 rows
+    with pytest.raises(RuntimeError):
+        K().gemm_skinny_splitk(x[:4], w, part, 3)  # 3 does not divide 16 slabs
+    with pytest.raises(RuntimeError):
+        K().gemm_skinny_splitk(x[:4], w[:1000], part, 1)  # N not a multiple of 128
+
+
+@pytest.mark.parametrize("M", [300, 450])
+def test_gemm_splitk_rows_over_256(cuda, M):
+    """Decode batches above 256 rows (the engine's batch holds every KV slot,
+    ~450 for Qwen3-32B at TP4) take the 256-row tiles; their split-K partials
+    sum to torch's fp32 product."""
+    g = torch.Generator().manual_seed(M)
+    for N, Kd in ((1024, 2048), (5120, 2048)):
+        x = torch.randn((M, Kd), generator=g).to(BF).to(cuda)
+        w = (torch.randn((N, Kd), generator=g) * 0.02).to(BF).to(cuda)
+        ref = x.float() @ w.float().t()
+        for splits in (1, 2, 4):
+            part = torch.empty((splits, M, N), dtype=torch.float32, device=cuda)
+            K().gemm_splitk(x, w, part, splits)
+            err = (part.sum(0) - ref).abs().max().item()
+            assert err <= 1e-3 * ref.abs().max().item() + 1e-4, (N, splits, err)
