@@ -35,7 +35,7 @@ SIGNATURES: dict[str, tuple] = {
     "aacc_paged_decode_attention_noalloc": (I32, [P, P, P, P, I64, P, I64, P, P, I32, I64, I32, I32, I32, F32, I32,
                                                   I64, P]),
     "aacc_paged_decode_noalloc_capacity_bytes": (I64, []),
-    "aacc_prefill_attention": (I32, [P, P, P, P, I64, P, I64, P, P, P, I64, I64, I32, I32, I32, F32, P]),
+    "aacc_prefill_attention": (I32, [P, P, I64, P, P, I64, P, I64, P, P, P, I64, I64, I32, I32, I32, F32, P]),
     "aacc_prefill_attention_mma": (I32, [P, P, P, P, I64, P, I64, P, P, P, I64, I64, I32, I32, I32, F32, P]),
     "aacc_rmsnorm": (I32, [P, P, P, I64, I64, F32, P]),
     "aacc_add_rmsnorm": (I32, [P, P, P, P, I64, I64, F32, P]),

@@ -61,19 +61,42 @@ unsigned* device_error_ptr() {
 
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
+static int load_encoder() {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return set_error(AACC_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  return AACC_OK;
+}
+
+int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1_bytes,
+                 uint64_t stride2_bytes, uint32_t box0, uint32_t box1, uint32_t box2, bool swizzle128) {
+  if (int st = load_encoder()) return st;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (stride1_bytes & 15) != 0 || (stride2_bytes & 15) != 0)
+    return set_error(AACC_ERR_INVALID, "TMA operand must be 16-byte aligned (base %p, strides %llu %llu)", base,
+                     (unsigned long long)stride1_bytes, (unsigned long long)stride2_bytes);
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  cuuint32_t box[3] = {box0, box1, box2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(AACC_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu x %llu box %u x %u x %u",
+                     (int)r, (unsigned long long)d0, (unsigned long long)d1, (unsigned long long)d2, box0, box1, box2);
+  return AACC_OK;
+}
+
 int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                  uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_encode) {
-      void* fn = nullptr;
-      cudaDriverEntryPointQueryResult q;
-      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
-          q != cudaDriverEntryPointSuccess || !fn)
-        return set_error(AACC_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
-      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    }
-  }
+  if (int st = load_encoder()) return st;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (row_stride_bytes & 15) != 0)
     return set_error(AACC_ERR_INVALID, "TMA operand must be 16-byte aligned (base %p, row stride %llu)", base,
                      (unsigned long long)row_stride_bytes);

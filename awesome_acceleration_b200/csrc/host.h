@@ -14,6 +14,12 @@ namespace aacc {
 int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                  uint32_t box_inner, uint32_t box_outer, bool swizzle128);
 
+// 3-D bf16 tensor map: d0 contiguous elements, d1 and d2 strided by
+// stride1 / stride2 bytes; box of box0 x box1 x box2 elements, written to
+// shared memory d0-fastest (row index = i2 * box1 + i1 when box0 fills a row).
+int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1_bytes,
+                 uint64_t stride2_bytes, uint32_t box0, uint32_t box1, uint32_t box2, bool swizzle128);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // Programmatic dependent launch: every kernel of this library is launched with

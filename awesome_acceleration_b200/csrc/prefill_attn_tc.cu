@@ -4,19 +4,23 @@
 //
 // One CTA per (pair of query tiles, kv head, sequence).  A tile's 128 MMA
 // rows are 128 / G query positions times the G query heads that share the kv
-// head (row r = head g * P + position p, P = 128 / G), so every K/V byte is
+// head (row r = position p * G + head g, P = 128 / G), so every K/V byte is
 // read once per kv head, not once per query head; the two tiles (A: positions
-// [qs, qs + P), B: the next P) share every K/V tile.  Per 128-key tile:
+// [qs, qs + P), B: the next P) share every K/V tile.  Each Q tile arrives by
+// TMA as two 3-D boxes (64 dims x G heads x P tokens) next to the first K
+// tile.  Per 128-key tile:
 //
 //   producer warp   TMA: K and V tiles (two 64-column halves each, 128-byte
 //                   swizzle) from the paged pool into a ring of three 32 KB
-//                   slots, in the order K0 V0 K1 V1 ...: a K slot is free
-//                   once both tiles' S used it, a V slot once both P.V did;
-//   MMA warp        S_t = Q_t K^T into tile t's TMEM score columns, and, once
-//                   tile t's softmax group has written P, O_t += P V into its
-//                   TMEM accumulator (V read as an MN-major operand, in
-//                   place), in the order S_A S_B | PV_A S_A' PV_B S_B' | ...
-//                   so one group's softmax overlaps the other's MMAs;
+//                   slots, K one tile ahead of V (K0 K1 V0 K2 V1 K3 V2 ...):
+//                   a K slot is free once both tiles' S used it, a V slot
+//                   once both P.V did;
+//   MMA warp        S_t(i+1) = Q_t K_{i+1}^T into tile t's TMEM score columns
+//                   as soon as tile t's softmax group has read S_t(i) into
+//                   registers (so it runs under that group's exponentials),
+//                   and O_t += P_t(i) V_i into its TMEM accumulator once the
+//                   group has written P (V read as an MN-major operand, in
+//                   place): S_A' S_B' PV_A PV_B per key tile;
 //   softmax groups  4 warps per tile, one thread per row: S from TMEM, causal
 //                   mask key_pos <= query_pos (query p of the chunk sits at
 //                   ctx_start + tile start + p) on the tiles that cross the
@@ -55,7 +59,9 @@ struct FlashSmem {
   uint8_t p[2][2][kFHalf];          // per tile, P: 128 rows x 128 keys as two 64-key halves
   uint64_t full[kFSlots];
   uint64_t empty[kFSlots];
+  uint64_t q_full;                  // both Q tiles landed
   uint64_t s_full[2];               // per tile: S ready
+  uint64_t s_free[2];               // per tile: S read into registers (its TMEM may be overwritten)
   uint64_t p_full[2];               // per tile: P written, O corrected
   uint64_t pv_done[2];              // per tile: O += P V done
   uint32_t tmem_slot;
@@ -72,7 +78,7 @@ __device__ __forceinline__ float fast_exp2(float x) {
 template <int G>
 __global__ void __launch_bounds__(kFThreads, 1)
     flash_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-                         const bf16* __restrict__ q, bf16* __restrict__ out, const int32_t* __restrict__ bt,
+                         const __grid_constant__ CUtensorMap tmq, bf16* __restrict__ out, const int32_t* __restrict__ bt,
                          int64_t max_blocks, const int64_t* __restrict__ seq_rows, const int32_t* __restrict__ cu_q,
                          const int32_t* __restrict__ ctx_start, int Hq, int Hkv, int bs, int64_t num_blocks,
                          int n_pairs, float scale_log2, unsigned* err) {
@@ -110,8 +116,10 @@ __global__ void __launch_bounds__(kFThreads, 1)
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], 1);
     }
+    mbar_init(&sm.q_full, 1);
     for (int t = 0; t < 2; ++t) {
       mbar_init(&sm.s_full[t], 1);
+      mbar_init(&sm.s_free[t], kFGroupWarps * 32);
       mbar_init(&sm.p_full[t], kFGroupWarps * 32);
       mbar_init(&sm.pv_done[t], 1);
     }
@@ -124,19 +132,6 @@ __global__ void __launch_bounds__(kFThreads, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if (warp < kFSoftmaxWarps) {
-    // Q rows of this group's tile into shared memory (K-major, 128-byte
-    // swizzle): row r = head g * P + position p.
-    const int t = warp / kFGroupWarps, r = threadIdx.x % 128, g = r / P, p = r % P;
-    const bool valid = p < (t ? rows_b : rows_a);
-    const bf16* src = q + ((q0 + qs0 + t * P + (valid ? p : 0)) * Hq + (int64_t)kvh * G + g) * kFD;
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      const uint4 v = valid ? reinterpret_cast<const uint4*>(src)[c] : make_uint4(0, 0, 0, 0);
-      *reinterpret_cast<uint4*>(sm.q[t][c >> 3] + swz128(r, c & 7)) = v;
-    }
-    fence_proxy_async();  // the tensor core reads these generic-proxy writes
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -146,27 +141,39 @@ __global__ void __launch_bounds__(kFThreads, 1)
   if (warp == kFSoftmaxWarps) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
+      tma_prefetch_desc(&tmq);
       tma_prefetch_desc(&tmk);
       tma_prefetch_desc(&tmv);
+      // Q tiles (K-major, 128-byte swizzle; row = position * G + head): rows
+      // past the chunk hold other tokens (or zeros past the last) and are
+      // never stored.
+      mbar_arrive_expect_tx(&sm.q_full, (have_b ? 4 : 2) * kFHalf);
+      for (int t = 0; t < (have_b ? 2 : 1); ++t)
+        for (int h = 0; h < 2; ++h)
+          tma_load_3d(sm.q[t][h], &tmq, &sm.q_full, 64 * h, kvh * G, (int)(q0 + qs0 + t * P));
       const int32_t* btrow = bt + row * max_blocks;
-      // unit u: K (u even) or V (u odd) of key tile u / 2, into slot u % 3
+      // unit u into slot u % 3: K_0, then K_{j+1}, V_j for j = 0 .. nkv-2, then V_{nkv-1}
       int issued = 0;
       for (int u = 0; u < 2 * nkv; ++u) {
         const int sl = u % kFSlots;
         if (u >= kFSlots && !mbar_wait(&sm.empty[sl], ((u / kFSlots) - 1) & 1, err, abort)) break;
-        const int64_t t0 = (int64_t)(u >> 1) * kFKeys;
+        const int w = u - 1;
+        const bool is_v = u > 0 && (w >= 2 * (nkv - 1) || (w & 1));
+        const int tile = u == 0 ? 0 : (w >= 2 * (nkv - 1) ? nkv - 1 : (w >> 1) + (is_v ? 0 : 1));
+        const int64_t t0 = (int64_t)tile * kFKeys;
         int64_t blk = btrow[t0 / bs];
         if (blk < 0 || blk >= num_blocks) {
           report(err, ERR_BLOCK_OOB);
           blk = 0;
         }
         const int r = (int)((blk * Hkv + kvh) * bs + t0 % bs);
-        const CUtensorMap* tm = (u & 1) ? &tmv : &tmk;
+        const CUtensorMap* tm = is_v ? &tmv : &tmk;
         mbar_arrive_expect_tx(&sm.full[sl], 2 * kFHalf);
         tma_load_2d(sm.kv[sl][0], tm, &sm.full[sl], 0, r);
         tma_load_2d(sm.kv[sl][1], tm, &sm.full[sl], 64, r);
         ++issued;
       }
+      mbar_wait(&sm.q_full, 0, err, nullptr);
       for (int sl = 0; sl < kFSlots && sl < issued; ++sl) {  // no copy in flight at exit
         const int last = sl + ((issued - 1 - sl) / kFSlots) * kFSlots;
         mbar_wait(&sm.full[sl], (last / kFSlots) & 1, err, nullptr);
@@ -174,19 +181,20 @@ __global__ void __launch_bounds__(kFThreads, 1)
     }
   } else if (warp == kFSoftmaxWarps + 1) {
     // ---------------- MMA issuer ----------------
-    // Tensor-pipe order: S_A(0) S_B(0) | PV_A(i) S_A(i+1) PV_B(i) S_B(i+1) | ...
-    // so each group's softmax overlaps the other group's MMAs.  Tile B's
+    // Per key tile i: S_A(i+1) S_B(i+1) (each once its group has read S(i))
+    // then PV_A(i) PV_B(i) (each once its group has written P(i)).  Tile B's
     // positions follow tile A's, so B uses every key tile A uses (nt_b >= nt_a).
     if (lane == 0) {
       constexpr uint32_t id_s = umma_idesc_m128(kFKeys, false);  // S = Q K^T: both K-major (over dims)
       constexpr uint32_t id_pv = umma_idesc_m128(kFD, true);     // O += P V: V is N(dims)-major
-      auto wait_unit = [&](int u) -> bool {
-        if (!mbar_wait(&sm.full[u % kFSlots], (u / kFSlots) & 1, err, abort)) return false;
+      auto wait_bar = [&](uint64_t* bar, int phase) -> bool {
+        if (!mbar_wait(bar, phase & 1, err, abort)) return false;
         tc_fence_after();
         return true;
       };
-      auto issue_s = [&](int t, int i) {
-        const uint32_t qb = smem_u32(sm.q[t][0]), kb = smem_u32(sm.kv[(2 * i) % kFSlots][0]);
+      auto wait_unit = [&](int u) { return wait_bar(&sm.full[u % kFSlots], u / kFSlots); };
+      auto issue_s = [&](int t, int u) {
+        const uint32_t qb = smem_u32(sm.q[t][0]), kb = smem_u32(sm.kv[u % kFSlots][0]);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // 16 dims per step
           const uint32_t off = (uint32_t)((kk >> 2) * kFHalf + (kk & 3) * 32);
@@ -194,10 +202,8 @@ __global__ void __launch_bounds__(kFThreads, 1)
         }
         umma_commit(&sm.s_full[t]);
       };
-      auto issue_pv = [&](int t, int i) -> bool {
-        if (!mbar_wait(&sm.p_full[t], i & 1, err, abort)) return false;
-        tc_fence_after();
-        const uint32_t pb = smem_u32(sm.p[t][0]), vb = smem_u32(sm.kv[(2 * i + 1) % kFSlots][0]);
+      auto issue_pv = [&](int t, int i, int u) {
+        const uint32_t pb = smem_u32(sm.p[t][0]), vb = smem_u32(sm.kv[u % kFSlots][0]);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // 16 keys per step
           const uint64_t a = umma_desc_sw128(pb + (uint32_t)((kk >> 2) * kFHalf + (kk & 3) * 32));
@@ -205,26 +211,38 @@ __global__ void __launch_bounds__(kFThreads, 1)
           umma_bf16(tmem + 256 + 128 * t, a, b, id_pv, (i | kk) != 0);
         }
         umma_commit(&sm.pv_done[t]);
-        return true;
       };
-      bool ok = nkv > 0 && wait_unit(0);
+      bool ok = nkv > 0 && wait_bar(&sm.q_full, 0) && wait_unit(0);  // Q, K_0
       if (ok) {
         if (nt_a > 0) issue_s(0, 0);
         if (have_b) issue_s(1, 0);
-        umma_commit(&sm.empty[0]);  // K_0 consumed
+        umma_commit(&sm.empty[0]);
       }
       for (int i = 0; ok && i < nkv; ++i) {
-        const bool more = i + 1 < nkv;
-        if (!(ok = wait_unit(2 * i + 1))) break;  // V_i
-        if (i < nt_a && !(ok = issue_pv(0, i))) break;
-        if (more && !(ok = wait_unit(2 * i + 2))) break;  // K_{i+1}
-        if (more && i + 1 < nt_a) issue_s(0, i + 1);
-        if (have_b && i < nt_b && !(ok = issue_pv(1, i))) break;
-        umma_commit(&sm.empty[(2 * i + 1) % kFSlots]);  // V_i consumed
-        if (more) {
-          if (have_b && i + 1 < nt_b) issue_s(1, i + 1);
-          umma_commit(&sm.empty[(2 * i + 2) % kFSlots]);  // K_{i+1} consumed
+        if (i + 1 < nkv) {  // K_{i+1} is unit 2i + 1
+          const int uk = 2 * i + 1;
+          if (!(ok = wait_unit(uk))) break;
+          if (i + 1 < nt_a) {
+            if (!(ok = wait_bar(&sm.s_free[0], i))) break;
+            issue_s(0, uk);
+          }
+          if (have_b && i + 1 < nt_b) {
+            if (!(ok = wait_bar(&sm.s_free[1], i))) break;
+            issue_s(1, uk);
+          }
+          umma_commit(&sm.empty[uk % kFSlots]);  // K_{i+1} consumed
         }
+        const int uv = 2 * i + 1 + (i + 1 < nkv ? 1 : 0);  // V_i
+        if (!(ok = wait_unit(uv))) break;
+        if (i < nt_a) {
+          if (!(ok = wait_bar(&sm.p_full[0], i))) break;
+          issue_pv(0, i, uv);
+        }
+        if (have_b && i < nt_b) {
+          if (!(ok = wait_bar(&sm.p_full[1], i))) break;
+          issue_pv(1, i, uv);
+        }
+        umma_commit(&sm.empty[uv % kFSlots]);  // V_i consumed
       }
     }
   } else {
@@ -233,7 +251,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     // independent, so they need no masking: only tiles that cross the causal
     // diagonal are masked.  The running maximum is kept on raw scores (the
     // scale is positive), so each exponent is one FFMA + EX2.
-    const int t = warp / kFGroupWarps, r = threadIdx.x % 128, p = r % P;
+    const int t = warp / kFGroupWarps, r = threadIdx.x % 128, p = r / G;
     const int qs = qs0 + t * P, rows_here = t ? rows_b : rows_a, ntiles = t ? nt_b : nt_a;
     const bool row_valid = p < rows_here;
     const int pos = (int)(c0 + qs + p), pos_min = (int)(c0 + qs);
@@ -255,6 +273,8 @@ __global__ void __launch_bounds__(kFThreads, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) sv[32 * c + j] = tv[j];
       }
+      tc_fence_before();
+      mbar_arrive(&sm.s_free[t]);  // the MMA may now overwrite S_t with the next tile's scores
       const int k0 = i * kFKeys;
       if (k0 + kFKeys - 1 > pos_min) {  // tile crosses the diagonal (warp-uniform)
 #pragma unroll
@@ -321,7 +341,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     if (ok && ntiles > 0 && mbar_wait(&sm.pv_done[t], (ntiles - 1) & 1, err, abort)) {
       tc_fence_after();
       const float il = l > 0.f ? 1.f / l : 0.f;
-      const int g = r / P;
+      const int g = r % G;
       bf16* dst = out + ((q0 + qs + p) * Hq + (int64_t)kvh * G + g) * kFD;
 #pragma unroll 1
       for (int c = 0; c < kFD / 16; ++c) {
@@ -364,12 +384,12 @@ static bool prefill_use_mma() {
 
 extern "C" {
 
-int aacc_prefill_attention(const void* q, void* out, const void* k_cache, const void* v_cache, int64_t num_blocks,
-                           const int32_t* block_tables, int64_t max_blocks, const int64_t* seq_rows, const int32_t* cu_q,
-                           const int32_t* ctx_start, int64_t num_seqs, int64_t max_q_len, int num_q_heads,
-                           int num_kv_heads, int block_size, float scale, cudaStream_t stream) {
+int aacc_prefill_attention(const void* q, void* out, int64_t num_tokens, const void* k_cache, const void* v_cache,
+                           int64_t num_blocks, const int32_t* block_tables, int64_t max_blocks, const int64_t* seq_rows,
+                           const int32_t* cu_q, const int32_t* ctx_start, int64_t num_seqs, int64_t max_q_len,
+                           int num_q_heads, int num_kv_heads, int block_size, float scale, cudaStream_t stream) {
   if (num_seqs < 0 || max_q_len < 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads || block_size <= 0 ||
-      block_size % 64 || num_blocks <= 0 || max_blocks <= 0)
+      block_size % 64 || num_blocks <= 0 || max_blocks <= 0 || num_tokens < 0 || max_q_len > num_tokens)
     return set_error(AACC_ERR_INVALID, "prefill_attention: bad sizes");
   const int G = num_q_heads / num_kv_heads;
   // The tensor-core kernel takes 128-key tiles (block sizes that are multiples
@@ -380,16 +400,20 @@ int aacc_prefill_attention(const void* q, void* out, const void* k_cache, const 
                                       ctx_start, num_seqs, max_q_len, num_q_heads, num_kv_heads, block_size, scale,
                                       stream);
   if (num_seqs == 0 || max_q_len == 0) return AACC_OK;
-  if (num_seqs > 65535) return set_error(AACC_ERR_UNSUPPORTED, "prefill_attention: too many sequences per call");
+  if (num_seqs > 65535 || num_tokens >= (int64_t(1) << 31))
+    return set_error(AACC_ERR_UNSUPPORTED, "prefill_attention: too many sequences or tokens per call");
   const int64_t rows = num_blocks * num_kv_heads * block_size;
   if (rows >= (int64_t(1) << 31)) return set_error(AACC_ERR_UNSUPPORTED, "prefill_attention: pool too large");
   if (!aligned16(q) || !aligned16(out)) return set_error(AACC_ERR_INVALID, "prefill_attention: q/out must be 16-byte aligned");
-  CUtensorMap tmk, tmv;
+  const int P = 128 / G;
+  CUtensorMap tmk, tmv, tmq;
   int st = make_tmap_2d(&tmk, k_cache, kFD, rows, kFD * 2, 64, kFKeys, true);
   if (st) return st;
   st = make_tmap_2d(&tmv, v_cache, kFD, rows, kFD * 2, 64, kFKeys, true);
   if (st) return st;
-  const int P = 128 / G;
+  // q as [token][head][dim]: boxes of 64 dims x G heads x P tokens
+  st = make_tmap_3d(&tmq, q, kFD, num_q_heads, num_tokens, kFD * 2, (uint64_t)num_q_heads * kFD * 2, 64, G, P, true);
+  if (st) return st;
   const int n_pairs = (int)((max_q_len + 2 * P - 1) / (2 * P));
   const size_t smem = sizeof(FlashSmem) + 1024;
   dim3 grid(n_pairs, num_kv_heads, (unsigned)num_seqs);
@@ -397,7 +421,7 @@ int aacc_prefill_attention(const void* q, void* out, const void* k_cache, const 
 #define AACC_LAUNCH_FLASH(GG)                                                                                      \
   {                                                                                                                \
     set_smem_once<flash_prefill_kernel<GG>>((int)smem);                                                            \
-    le = launch_k(flash_prefill_kernel<GG>, grid, dim3(kFThreads), smem, stream, tmk, tmv, (const bf16*)q,         \
+    le = launch_k(flash_prefill_kernel<GG>, grid, dim3(kFThreads), smem, stream, tmk, tmv, tmq,                    \
                   (bf16*)out, block_tables, max_blocks, seq_rows, cu_q, ctx_start, num_q_heads, num_kv_heads,       \
                   block_size, num_blocks, n_pairs, scale * kLog2e, device_error_ptr());                            \
   }

@@ -92,7 +92,7 @@ def prefill_attention(q, k_cache, v_cache, block_tables, seq_rows, cu_q, ctx_sta
     if out is None:
         out = torch.empty_like(q)
     _lib.check(_lib_().aacc_prefill_attention(
-        _p(q), _p(out), _p(k_cache), _p(v_cache), nb, _p(block_tables), block_tables.shape[1], _p(seq_rows),
+        _p(q), _p(out), T, _p(k_cache), _p(v_cache), nb, _p(block_tables), block_tables.shape[1], _p(seq_rows),
         _p(cu_q), _p(ctx_start), seq_rows.shape[0], max_q_len, hq, hkv, bs, scale, _stream()),
         "prefill_attention")
     return out
@@ -214,7 +214,10 @@ def splitk_reduce(partial, splits: int, out):
 # ---------------------------------------------------------------- small-batch decode projections
 SKINNY_MAX_ROWS = 64      # what the kernels take
 SKINNY_DEFAULT_ROWS = 32  # batches the engine sends through them
-SKINNY_FUSED_ROWS = 8     # up to here the QKV / SiLU epilogues run in the GEMM's last split CTAs
+# Batches up to this run the QKV / SiLU epilogues in the GEMM's last split CTAs.  Off: on
+# B200 the serial tail of the last CTA cost more than the separate epilogue launch at
+# every batch measured (Qwen3-0.6B shapes, B = 1: 30.5 vs 27.4 us per layer).
+SKINNY_FUSED_ROWS = 0
 SKINNY_TARGET_CTAS = 296      # QKV / gate-up grids: about two CTAs per SM
 SKINNY_TARGET_CTAS_ROW = 148  # o / down grids: fewer splits for the norm kernel to sum
 

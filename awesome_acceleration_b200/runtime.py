@@ -223,6 +223,7 @@ class Qwen3Runtime:
         self.chunk = prefill_chunk_tokens
         self.cluster_gemm = os.environ.get("AACC_CLUSTER_GEMM", "0") == "1"
         self.skinny_rows = int(os.environ.get("AACC_SKINNY_ROWS", str(K.SKINNY_DEFAULT_ROWS)))
+        self.skinny_fused_rows = int(os.environ.get("AACC_SKINNY_FUSED_ROWS", str(K.SKINNY_FUSED_ROWS)))
         self.device = embed.device
         self.max_context = kv.max_blocks * kv.block_size
         self.buf = _DecodeBuffers(max_batch, hidden, self.Hq, self.I, self.vocab_local, tp, self.max_context,
@@ -265,10 +266,10 @@ class Qwen3Runtime:
         """Decode batches of at most `skinny_rows` rows (AACC_SKINNY_ROWS)
         run the small-batch GEMMs: weights as the MMA's 128-row operand, a
         third of the shared memory per CTA, so two or three CTAs share an SM
-        and a projection's weight stream overlaps the kernel before it; up to
-        SKINNY_FUSED_ROWS rows the QKV / SiLU epilogues finish in the same
-        launch (beyond that the tile's last CTA would walk too many rows, and
-        the epilogue kernels run them in parallel)."""
+        and a projection's weight stream overlaps the kernel before it.  The
+        QKV / SiLU epilogues run in the split-K epilogue kernels, or, for
+        batches up to AACC_SKINNY_FUSED_ROWS (default 0: measured slower), in
+        the GEMM's last split CTA of each tile."""
         return part is not None and 0 < M <= min(self.skinny_rows, K.SKINNY_MAX_ROWS) and not self.cluster_gemm
 
     def _skinny_part(self, M, w, part, target):
@@ -282,7 +283,7 @@ class Qwen3Runtime:
         M = x.shape[0]
         if self._skinny(M, part):
             sp, pv = self._skinny_part(M, lw.wqkv, part, K.SKINNY_TARGET_CTAS)
-            if M <= K.SKINNY_FUSED_ROWS:
+            if M <= self.skinny_fused_rows:
                 K.skinny_qkv_norm_rope_store(x, lw.wqkv, pv, sp, self.buf.sk_cnt, lw.q_norm, lw.k_norm, self.eps,
                                              positions, self.rope, slot_map, kv.k[i], kv.v[i], self.Hq, q_out=q)
             else:
@@ -310,7 +311,7 @@ class Qwen3Runtime:
         M = x.shape[0]
         if self._skinny(M, part):
             sp, pv = self._skinny_part(M, lw.w_gate_up, part, K.SKINNY_TARGET_CTAS)
-            if M <= K.SKINNY_FUSED_ROWS:
+            if M <= self.skinny_fused_rows:
                 K.skinny_silu_mul(x, lw.w_gate_up, pv, sp, self.buf.sk_cnt, act)
             else:
                 K.gemm_skinny_splitk(x, lw.w_gate_up, pv, sp)

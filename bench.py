@@ -455,12 +455,14 @@ def run_hbm(args, device):
 # --------------------------------------------------------------------------- prefill attention (tensor pipe)
 def run_prefill_attn(args, device):
     """Causal prefill attention over the paged cache on one packed chunk of
-    the cfg2 prefill: 32 sequences x 1024 prompt tokens (32,768 query tokens),
-    16 / 8 heads, block 256, a permuted block pool.  FLOPs = 4 * 128 * Hq *
-    sum over queries of the keys each attends (causal).  AACC_PREFILL_ATTN=mma
-    times the mma.sync kernel instead of the tcgen05 one."""
+    the cfg2 prefill: 32 sequences x 1024 prompt tokens (32,768 query tokens;
+    --prefill-len L packs 32768 / L prompts of L tokens), 16 / 8 heads, block
+    256, a permuted block pool.  FLOPs = 4 * 128 * Hq * sum over queries of
+    the keys each attends (causal).  AACC_PREFILL_ATTN=mma times the mma.sync
+    kernel instead of the tcgen05 one."""
     from awesome_acceleration_b200 import _lib, kernels as Kk
-    n, L = (8, 1024) if args.small else (32, 1024)
+    L = args.prefill_len
+    n = (8 if args.small else 32) * 1024 // L
     hq, hkv, bs = 16, 8, 256
     g = torch.Generator().manual_seed(11)
     nb = n * (L // bs) + 8
@@ -499,7 +501,8 @@ def run_prefill_attn(args, device):
     return {"metric": f"causal prefill attention TFLOP/s ({n} x {L} tokens, 16/8 heads)", "value": round(ach, 1),
             "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "cfg2 prefill chunk attention", "kernel": kernel, "l2": "K/V 1 GB > L2"},
+            "config": {"workload": "cfg2 prefill chunk attention", "prompt_len": L, "kernel": kernel,
+                       "l2": "q 134 MB + K/V 143 MB > L2"},
             "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": round(ach / pk["bf16_tflops"], 3), "traffic": None, "peak_kind": kind},
             "gpu_launches": args.steps + args.warmup, "clocks": clk.summary()}
@@ -1062,6 +1065,8 @@ def main():
                     help="cfg2: skip the cfg4 (Qwen3-8B) tensor-parallel block at TP = the world")
     ap.add_argument("--decode", action="store_true", help="gemm workload: decode-batch shapes")
     ap.add_argument("--batch", type=int, default=0, help="gemm --decode: batch rows (default 256)")
+    ap.add_argument("--prefill-len", type=int, default=1024, choices=[256, 512, 1024, 2048, 4096, 8192],
+                    help="prefill-attn: prompt length of the 32,768-token chunk")
     ap.add_argument("--proj-shapes", default="0.6b", choices=["0.6b", "8b"],
                     help="gemm --decode: Qwen3-0.6B (28 layers) or Qwen3-8B (8 layers) projection shapes")
     ap.add_argument("--no-cluster", action="store_true", help="gemm --decode: skip the cluster variant")

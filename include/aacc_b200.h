@@ -128,16 +128,17 @@ int aacc_paged_decode_attention_noalloc(const void* q, void* out, const void* k_
 int64_t aacc_paged_decode_noalloc_capacity_bytes(void);
 
 /* Causal (chunked) prefill attention over the paged cache.  Sequence s owns
- * query rows [cu_q[s], cu_q[s+1]) of q/out ([T][num_q_heads][128]) at
- * positions ctx_start[s] + i; its K/V (earlier chunks and this chunk) are
- * already in the cache under block-table row seq_rows[s].  max_q_len bounds
- * cu_q[s+1]-cu_q[s].  Replaces flash_attn_varlen_func (llm.py:178-184,
- * llm_tp.py:471-477) and flash_attn_func (model/model.py:253-254). */
-int aacc_prefill_attention(const void* q, void* out, const void* k_cache, const void* v_cache,
-                           int64_t num_blocks, const int32_t* block_tables, int64_t max_blocks,
-                           const int64_t* seq_rows, const int32_t* cu_q, const int32_t* ctx_start,
-                           int64_t num_seqs, int64_t max_q_len, int num_q_heads, int num_kv_heads,
-                           int block_size, float scale, cudaStream_t stream);
+ * query rows [cu_q[s], cu_q[s+1]) of q/out ([num_tokens][num_q_heads][128],
+ * cu_q[num_seqs] <= num_tokens) at positions ctx_start[s] + i; its K/V
+ * (earlier chunks and this chunk) are already in the cache under
+ * block-table row seq_rows[s].  max_q_len bounds cu_q[s+1]-cu_q[s].
+ * Replaces flash_attn_varlen_func (llm.py:178-184, llm_tp.py:471-477) and
+ * flash_attn_func (model/model.py:253-254). */
+int aacc_prefill_attention(const void* q, void* out, int64_t num_tokens, const void* k_cache,
+                           const void* v_cache, int64_t num_blocks, const int32_t* block_tables,
+                           int64_t max_blocks, const int64_t* seq_rows, const int32_t* cu_q,
+                           const int32_t* ctx_start, int64_t num_seqs, int64_t max_q_len, int num_q_heads,
+                           int num_kv_heads, int block_size, float scale, cudaStream_t stream);
 
 /* The same computation on mma.sync m16n8k16 with one CTA per query head
  * (block_size % 64 == 0).  aacc_prefill_attention runs it for block sizes
