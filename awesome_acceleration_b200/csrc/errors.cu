@@ -61,6 +61,19 @@ unsigned* device_error_ptr() {
 
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
+int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& c = cache[dev & 63];
+  if (c == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    c = n;
+  }
+  return c;
+}
+
 static int load_encoder() {
   std::lock_guard<std::mutex> lk(g_mu);
   if (!g_encode) {

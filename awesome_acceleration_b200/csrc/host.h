@@ -20,6 +20,9 @@ int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t ou
 int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1_bytes,
                  uint64_t stride2_bytes, uint32_t box0, uint32_t box1, uint32_t box2, bool swizzle128);
 
+// Streaming multiprocessors of the current device (cached per device).
+int sm_count();
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // Programmatic dependent launch: every kernel of this library is launched with

@@ -38,6 +38,8 @@
 //
 // Every wait is bounded; a wait that runs out reports ERR_WAIT_TIMEOUT and
 // the CTA stops issuing work, drains its own copies and frees TMEM.
+#include <algorithm>
+
 #include "common.cuh"
 #include "host.h"
 #include "tcgen05.cuh"
@@ -59,11 +61,13 @@ struct FlashSmem {
   uint8_t p[2][2][kFHalf];          // per tile, P: 128 rows x 128 keys as two 64-key halves
   uint64_t full[kFSlots];
   uint64_t empty[kFSlots];
-  uint64_t q_full;                  // both Q tiles landed
+  uint64_t q_full;                  // the item's Q tiles landed
+  uint64_t q_free;                  // the item's last S done: Q buffers may be refilled
   uint64_t s_full[2];               // per tile: S ready
   uint64_t s_free[2];               // per tile: S read into registers (its TMEM may be overwritten)
   uint64_t p_full[2];               // per tile: P written, O corrected
   uint64_t pv_done[2];              // per tile: O += P V done
+  uint64_t o_free[2];               // per tile: the item's O read out of TMEM
   uint32_t tmem_slot;
   int abort;
 };
@@ -75,41 +79,60 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// One work item: a pair of query tiles of one (sequence, kv head).  Items run
+// pair-major, heaviest (latest positions, most key tiles) first: item j has
+// pair n_pairs - 1 - j / (Hkv * n_seqs).  Returns false for a pair past the
+// end of its sequence's chunk.
+struct FlashItem {
+  int64_t q0, c0, row;
+  int kvh, qs0, q_len, rows_a, rows_b, nt_a, nt_b, nkv;
+  bool have_b, clamped;
+};
+
+template <int P>
+__device__ __forceinline__ bool flash_item(int j, int n_pairs, int Hkv, int n_seqs, const int32_t* __restrict__ cu_q,
+                                           const int32_t* __restrict__ ctx_start,
+                                           const int64_t* __restrict__ seq_rows, int64_t kv_cap, FlashItem& it) {
+  const int per_pair = Hkv * n_seqs;
+  const int pair = n_pairs - 1 - j / per_pair, rem = j % per_pair;
+  const int s = rem / Hkv;
+  it.kvh = rem % Hkv;
+  it.q0 = cu_q[s];
+  it.q_len = cu_q[s + 1] - (int)it.q0;
+  it.qs0 = pair * 2 * P;  // tile A: positions [qs0, qs0 + P); tile B: the next P
+  if (it.qs0 >= it.q_len) return false;
+  it.c0 = ctx_start[s];
+  it.row = seq_rows[s];
+  it.rows_a = min(P, it.q_len - it.qs0);
+  it.rows_b = it.qs0 + P < it.q_len ? min(P, it.q_len - it.qs0 - P) : 0;
+  it.nt_a = (int)((it.c0 + it.qs0 + it.rows_a - 1) / kFKeys) + 1;
+  it.nt_b = it.rows_b ? (int)((it.c0 + it.qs0 + P + it.rows_b - 1) / kFKeys) + 1 : 0;
+  it.clamped = it.nt_a > kv_cap || it.nt_b > kv_cap;
+  it.nt_a = min(it.nt_a, (int)kv_cap);
+  it.nt_b = min(it.nt_b, (int)kv_cap);
+  it.have_b = it.nt_b > 0;
+  it.nkv = max(it.nt_a, it.nt_b);
+  return true;
+}
+
+// Persistent: one CTA per SM walks items j = blockIdx.x, + gridDim.x, ...;
+// barriers and TMEM are set up once, and every barrier's phase runs on across
+// items, so an item's loads and first S start while the previous item's
+// softmax groups finish and store O.
 template <int G>
 __global__ void __launch_bounds__(kFThreads, 1)
     flash_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                          const __grid_constant__ CUtensorMap tmq, bf16* __restrict__ out, const int32_t* __restrict__ bt,
                          int64_t max_blocks, const int64_t* __restrict__ seq_rows, const int32_t* __restrict__ cu_q,
                          const int32_t* __restrict__ ctx_start, int Hq, int Hkv, int bs, int64_t num_blocks,
-                         int n_pairs, float scale_log2, unsigned* err) {
+                         int n_pairs, int n_seqs, float scale_log2, unsigned* err) {
   constexpr int P = 128 / G;  // query positions per tile
   extern __shared__ uint8_t smem_raw[];
   FlashSmem& sm = *reinterpret_cast<FlashSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   griddep_wait();
   griddep_launch();
-  const int pair = n_pairs - 1 - (int)blockIdx.x;  // heaviest tiles first
-  const int kvh = blockIdx.y;
-  const int64_t s = blockIdx.z;
-  const int64_t q0 = cu_q[s];
-  const int q_len = cu_q[s + 1] - (int)q0;
-  const int qs0 = pair * 2 * P;  // tile A: positions [qs0, qs0 + P); tile B: the next P
-  if (qs0 >= q_len) return;      // whole CTA, before any barrier or TMEM is set up
-  const int64_t c0 = ctx_start[s];
-  const int64_t row = seq_rows[s];
+  const int n_items = n_pairs * Hkv * n_seqs;
   const int64_t kv_cap = max_blocks * bs / kFKeys;  // key tiles the block table can hold
-  // rows and key tiles of tile A (a) and tile B (b)
-  const int rows_a = min(P, q_len - qs0);
-  const int rows_b = qs0 + P < q_len ? min(P, q_len - qs0 - P) : 0;
-  int nt_a = (int)((c0 + qs0 + rows_a - 1) / kFKeys) + 1;
-  int nt_b = rows_b ? (int)((c0 + qs0 + P + rows_b - 1) / kFKeys) + 1 : 0;
-  if (nt_a > kv_cap || nt_b > kv_cap) {
-    if (threadIdx.x == 0) report(err, ERR_CTX_OOB);
-    nt_a = min(nt_a, (int)kv_cap);
-    nt_b = min(nt_b, (int)kv_cap);
-  }
-  const bool have_b = nt_b > 0;
-  const int nkv = max(nt_a, nt_b);
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kFSlots; ++i) {
@@ -117,11 +140,13 @@ __global__ void __launch_bounds__(kFThreads, 1)
       mbar_init(&sm.empty[i], 1);
     }
     mbar_init(&sm.q_full, 1);
+    mbar_init(&sm.q_free, 1);
     for (int t = 0; t < 2; ++t) {
       mbar_init(&sm.s_full[t], 1);
       mbar_init(&sm.s_free[t], kFGroupWarps * 32);
       mbar_init(&sm.p_full[t], kFGroupWarps * 32);
       mbar_init(&sm.pv_done[t], 1);
+      mbar_init(&sm.o_free[t], kFGroupWarps * 32);
     }
     sm.abort = 0;
     fence_mbar_init();
@@ -144,46 +169,57 @@ __global__ void __launch_bounds__(kFThreads, 1)
       tma_prefetch_desc(&tmq);
       tma_prefetch_desc(&tmk);
       tma_prefetch_desc(&tmv);
-      // Q tiles (K-major, 128-byte swizzle; row = position * G + head): rows
-      // past the chunk hold other tokens (or zeros past the last) and are
-      // never stored.
-      mbar_arrive_expect_tx(&sm.q_full, (have_b ? 4 : 2) * kFHalf);
-      for (int t = 0; t < (have_b ? 2 : 1); ++t)
-        for (int h = 0; h < 2; ++h)
-          tma_load_3d(sm.q[t][h], &tmq, &sm.q_full, 64 * h, kvh * G, (int)(q0 + qs0 + t * P));
-      const int32_t* btrow = bt + row * max_blocks;
-      // unit u into slot u % 3: K_0, then K_{j+1}, V_j for j = 0 .. nkv-2, then V_{nkv-1}
-      int issued = 0;
-      for (int u = 0; u < 2 * nkv; ++u) {
-        const int sl = u % kFSlots;
-        if (u >= kFSlots && !mbar_wait(&sm.empty[sl], ((u / kFSlots) - 1) & 1, err, abort)) break;
-        const int w = u - 1;
-        const bool is_v = u > 0 && (w >= 2 * (nkv - 1) || (w & 1));
-        const int tile = u == 0 ? 0 : (w >= 2 * (nkv - 1) ? nkv - 1 : (w >> 1) + (is_v ? 0 : 1));
-        const int64_t t0 = (int64_t)tile * kFKeys;
-        int64_t blk = btrow[t0 / bs];
-        if (blk < 0 || blk >= num_blocks) {
-          report(err, ERR_BLOCK_OOB);
-          blk = 0;
+      int U = 0, nq = 0;  // K/V units issued, items whose Q was loaded (running over items)
+      bool ok = true;
+      for (int j = blockIdx.x; ok && j < n_items; j += gridDim.x) {
+        FlashItem it;
+        if (!flash_item<P>(j, n_pairs, Hkv, n_seqs, cu_q, ctx_start, seq_rows, kv_cap, it)) continue;
+        if (it.clamped) report(err, ERR_CTX_OOB);
+        // Q tiles (K-major, 128-byte swizzle; row = position * G + head), once
+        // the previous item's last S has read the buffers.  Rows past the
+        // chunk hold other tokens (or zeros past the last) and are never stored.
+        if (nq > 0 && !(ok = mbar_wait(&sm.q_free, (nq - 1) & 1, err, abort))) break;
+        mbar_arrive_expect_tx(&sm.q_full, (it.have_b ? 4 : 2) * kFHalf);
+        for (int t = 0; t < (it.have_b ? 2 : 1); ++t)
+          for (int h = 0; h < 2; ++h)
+            tma_load_3d(sm.q[t][h], &tmq, &sm.q_full, 64 * h, it.kvh * G, (int)(it.q0 + it.qs0 + t * P));
+        ++nq;
+        const int32_t* btrow = bt + it.row * max_blocks;
+        // unit u of the item: K_0, then K_{j+1}, V_j for j = 0 .. nkv-2, then V_{nkv-1}
+        for (int u = 0; u < 2 * it.nkv; ++u) {
+          const int sl = U % kFSlots;
+          if (U >= kFSlots && !(ok = mbar_wait(&sm.empty[sl], ((U / kFSlots) - 1) & 1, err, abort))) break;
+          const int w = u - 1;
+          const bool is_v = u > 0 && (w >= 2 * (it.nkv - 1) || (w & 1));
+          const int tile = u == 0 ? 0 : (w >= 2 * (it.nkv - 1) ? it.nkv - 1 : (w >> 1) + (is_v ? 0 : 1));
+          const int64_t t0 = (int64_t)tile * kFKeys;
+          int64_t blk = btrow[t0 / bs];
+          if (blk < 0 || blk >= num_blocks) {
+            report(err, ERR_BLOCK_OOB);
+            blk = 0;
+          }
+          const int r = (int)((blk * Hkv + it.kvh) * bs + t0 % bs);
+          const CUtensorMap* tm = is_v ? &tmv : &tmk;
+          mbar_arrive_expect_tx(&sm.full[sl], 2 * kFHalf);
+          tma_load_2d(sm.kv[sl][0], tm, &sm.full[sl], 0, r);
+          tma_load_2d(sm.kv[sl][1], tm, &sm.full[sl], 64, r);
+          ++U;
         }
-        const int r = (int)((blk * Hkv + kvh) * bs + t0 % bs);
-        const CUtensorMap* tm = is_v ? &tmv : &tmk;
-        mbar_arrive_expect_tx(&sm.full[sl], 2 * kFHalf);
-        tma_load_2d(sm.kv[sl][0], tm, &sm.full[sl], 0, r);
-        tma_load_2d(sm.kv[sl][1], tm, &sm.full[sl], 64, r);
-        ++issued;
       }
-      mbar_wait(&sm.q_full, 0, err, nullptr);
-      for (int sl = 0; sl < kFSlots && sl < issued; ++sl) {  // no copy in flight at exit
-        const int last = sl + ((issued - 1 - sl) / kFSlots) * kFSlots;
+      // No copy in flight at exit (normally the MMA thread has waited for all).
+      if (nq > 0) mbar_wait(&sm.q_full, (nq - 1) & 1, err, nullptr);
+      for (int sl = 0; sl < kFSlots && sl < U; ++sl) {
+        const int last = sl + ((U - 1 - sl) / kFSlots) * kFSlots;
         mbar_wait(&sm.full[sl], (last / kFSlots) & 1, err, nullptr);
       }
     }
   } else if (warp == kFSoftmaxWarps + 1) {
     // ---------------- MMA issuer ----------------
-    // Per key tile i: S_A(i+1) S_B(i+1) (each once its group has read S(i))
-    // then PV_A(i) PV_B(i) (each once its group has written P(i)).  Tile B's
-    // positions follow tile A's, so B uses every key tile A uses (nt_b >= nt_a).
+    // Per item: S_A(0) S_B(0); per key tile i: S_A(i+1) S_B(i+1) (each once
+    // its group has read S(i)) then PV_A(i) PV_B(i) (each once its group has
+    // written P(i); the item's first PV also once the group has read the
+    // previous item's O).  Tile B's positions follow tile A's, so B uses every
+    // key tile A uses (nt_b >= nt_a).
     if (lane == 0) {
       constexpr uint32_t id_s = umma_idesc_m128(kFKeys, false);  // S = Q K^T: both K-major (over dims)
       constexpr uint32_t id_pv = umma_idesc_m128(kFD, true);     // O += P V: V is N(dims)-major
@@ -192,7 +228,6 @@ __global__ void __launch_bounds__(kFThreads, 1)
         tc_fence_after();
         return true;
       };
-      auto wait_unit = [&](int u) { return wait_bar(&sm.full[u % kFSlots], u / kFSlots); };
       auto issue_s = [&](int t, int u) {
         const uint32_t qb = smem_u32(sm.q[t][0]), kb = smem_u32(sm.kv[u % kFSlots][0]);
 #pragma unroll
@@ -212,37 +247,55 @@ __global__ void __launch_bounds__(kFThreads, 1)
         }
         umma_commit(&sm.pv_done[t]);
       };
-      bool ok = nkv > 0 && wait_bar(&sm.q_full, 0) && wait_unit(0);  // Q, K_0
-      if (ok) {
-        if (nt_a > 0) issue_s(0, 0);
-        if (have_b) issue_s(1, 0);
-        umma_commit(&sm.empty[0]);
-      }
-      for (int i = 0; ok && i < nkv; ++i) {
-        if (i + 1 < nkv) {  // K_{i+1} is unit 2i + 1
-          const int uk = 2 * i + 1;
-          if (!(ok = wait_unit(uk))) break;
-          if (i + 1 < nt_a) {
-            if (!(ok = wait_bar(&sm.s_free[0], i))) break;
-            issue_s(0, uk);
+      // running counts: units consumed, items, and waits per tile on s_free / p_full / o_free
+      int V = 0, nq = 0, nsf[2] = {0, 0}, npf[2] = {0, 0}, nof[2] = {0, 0}, seen[2] = {0, 0};
+      bool ok = true;
+      for (int j = blockIdx.x; ok && j < n_items; j += gridDim.x) {
+        FlashItem it;
+        if (!flash_item<P>(j, n_pairs, Hkv, n_seqs, cu_q, ctx_start, seq_rows, kv_cap, it)) continue;
+        const int nkv = it.nkv, nt_a = it.nt_a, nt_b = it.nt_b;
+        const bool have_b = it.have_b;
+        if (!(ok = wait_bar(&sm.q_full, nq++))) break;
+        const int u0 = V++;  // K_0
+        if (!(ok = wait_bar(&sm.full[u0 % kFSlots], u0 / kFSlots))) break;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (t == 1 && !have_b) break;
+          if (seen[t] && !(ok = wait_bar(&sm.s_free[t], nsf[t]++))) break;  // previous item's last S read
+          issue_s(t, u0);
+        }
+        if (!ok) break;
+        if (nkv == 1) umma_commit(&sm.q_free);  // the item's last S: Q may be replaced
+        umma_commit(&sm.empty[u0 % kFSlots]);
+        for (int i = 0; ok && i < nkv; ++i) {
+          if (i + 1 < nkv) {
+            const int uk = V++;  // K_{i+1}
+            if (!(ok = wait_bar(&sm.full[uk % kFSlots], uk / kFSlots))) break;
+            if (i + 1 < nt_a) {
+              if (!(ok = wait_bar(&sm.s_free[0], nsf[0]++))) break;
+              issue_s(0, uk);
+            }
+            if (have_b && i + 1 < nt_b) {
+              if (!(ok = wait_bar(&sm.s_free[1], nsf[1]++))) break;
+              issue_s(1, uk);
+            }
+            if (i + 2 == nkv) umma_commit(&sm.q_free);
+            umma_commit(&sm.empty[uk % kFSlots]);  // K_{i+1} consumed
           }
-          if (have_b && i + 1 < nt_b) {
-            if (!(ok = wait_bar(&sm.s_free[1], i))) break;
-            issue_s(1, uk);
+          const int uv = V++;  // V_i
+          if (!(ok = wait_bar(&sm.full[uv % kFSlots], uv / kFSlots))) break;
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            if (i >= (t ? (have_b ? nt_b : 0) : nt_a)) continue;
+            if (i == 0 && seen[t] && !(ok = wait_bar(&sm.o_free[t], nof[t]++))) break;  // previous O read
+            if (!(ok = wait_bar(&sm.p_full[t], npf[t]++))) break;
+            issue_pv(t, i, uv);
           }
-          umma_commit(&sm.empty[uk % kFSlots]);  // K_{i+1} consumed
+          if (!ok) break;
+          umma_commit(&sm.empty[uv % kFSlots]);  // V_i consumed
         }
-        const int uv = 2 * i + 1 + (i + 1 < nkv ? 1 : 0);  // V_i
-        if (!(ok = wait_unit(uv))) break;
-        if (i < nt_a) {
-          if (!(ok = wait_bar(&sm.p_full[0], i))) break;
-          issue_pv(0, i, uv);
-        }
-        if (have_b && i < nt_b) {
-          if (!(ok = wait_bar(&sm.p_full[1], i))) break;
-          issue_pv(1, i, uv);
-        }
-        umma_commit(&sm.empty[uv % kFSlots]);  // V_i consumed
+        ++seen[0];
+        if (have_b) ++seen[1];
       }
     }
   } else {
@@ -251,106 +304,112 @@ __global__ void __launch_bounds__(kFThreads, 1)
     // independent, so they need no masking: only tiles that cross the causal
     // diagonal are masked.  The running maximum is kept on raw scores (the
     // scale is positive), so each exponent is one FFMA + EX2.
-    const int t = warp / kFGroupWarps, r = threadIdx.x % 128, p = r / G;
-    const int qs = qs0 + t * P, rows_here = t ? rows_b : rows_a, ntiles = t ? nt_b : nt_a;
-    const bool row_valid = p < rows_here;
-    const int pos = (int)(c0 + qs + p), pos_min = (int)(c0 + qs);
+    const int t = warp / kFGroupWarps, r = threadIdx.x % 128, p = r / G, g = r % G;
     const uint32_t lane_off = (uint32_t)((warp % kFGroupWarps) * 32) << 16;
     const uint32_t tS = tmem + 128 * t, tO = tmem + 256 + 128 * t;
-    float m = -INFINITY, l = 0.f;
+    int nsf = 0, npd = 0;  // waits on s_full / pv_done (running over items)
     bool ok = true;
-    for (int i = 0; i < ntiles; ++i) {
-      if (!mbar_wait(&sm.s_full[t], i & 1, err, abort)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      float sv[kFKeys];
-#pragma unroll
-      for (int c = 0; c < kFKeys / 32; ++c) {
-        float tv[32];
-        tmem_ld32(tS + lane_off + 32 * c, tv);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) sv[32 * c + j] = tv[j];
-      }
-      tc_fence_before();
-      mbar_arrive(&sm.s_free[t]);  // the MMA may now overwrite S_t with the next tile's scores
-      const int k0 = i * kFKeys;
-      if (k0 + kFKeys - 1 > pos_min) {  // tile crosses the diagonal (warp-uniform)
-#pragma unroll
-        for (int j = 0; j < kFKeys; ++j)
-          if (k0 + j > pos) sv[j] = -INFINITY;
-      }
-      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int j = 0; j < kFKeys; j += 4) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) mx[u] = fmaxf(mx[u], sv[j + u]);
-      }
-      // m: the row's reference maximum (raw score); it moves to the tile's
-      // maximum only when that exceeds it by more than 8 / scale_log2.
-      const float m_tile = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-      const float m_new = (m_tile - m) * scale_log2 > kFRescaleLog2 ? m_tile : m;  // m = -inf: moves
-      const float msc = (m_new == -INFINITY ? 0.f : m_new) * scale_log2;
-      const float alpha = m_new == m ? 1.f : fast_exp2(fmaf(m, scale_log2, -msc));  // m = -inf: 0
-      float rs[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int j = 0; j < kFKeys; j += 4) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          sv[j + u] = fast_exp2(fmaf(sv[j + u], scale_log2, -msc));
-          rs[u] += sv[j + u];
-        }
-      }
-      l = l * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
-      m = m_new;
-      // This tile's previous P.V must be done: it reads this tile's P
-      // buffer and updates O, which a rescale reads below.
-      if (i > 0) {
-        if (!mbar_wait(&sm.pv_done[t], (i - 1) & 1, err, abort)) {
+    for (int j = blockIdx.x; ok && j < n_items; j += gridDim.x) {
+      FlashItem it;
+      if (!flash_item<P>(j, n_pairs, Hkv, n_seqs, cu_q, ctx_start, seq_rows, kv_cap, it)) continue;
+      if (t == 1 && !it.have_b) continue;
+      const int qs = it.qs0 + t * P, ntiles = t ? it.nt_b : it.nt_a;
+      const bool row_valid = p < (t ? it.rows_b : it.rows_a);
+      const int pos = (int)(it.c0 + qs + p), pos_min = (int)(it.c0 + qs);
+      bf16* const dst = out + ((it.q0 + qs + p) * Hq + (int64_t)it.kvh * G + g) * kFD;
+      float m = -INFINITY, l = 0.f;
+      for (int i = 0; i < ntiles; ++i) {
+        if (!mbar_wait(&sm.s_full[t], (nsf++) & 1, err, abort)) {
           ok = false;
           break;
         }
         tc_fence_after();
-      }
-      if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {  // tcgen05.ld/st are warp-wide
-#pragma unroll 1
-        for (int c = 0; c < kFD / 16; ++c) {
-          float ov[16];
-          tmem_ld16(tO + lane_off + 16 * c, ov);
+        float sv[kFKeys];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) ov[j] *= alpha;
-          tmem_st16(tO + lane_off + 16 * c, ov);
+        for (int c = 0; c < kFKeys / 32; ++c)
+          tmem_ld32(tS + lane_off + 32 * c, *reinterpret_cast<float(*)[32]>(sv + 32 * c));
+        tc_fence_before();
+        mbar_arrive(&sm.s_free[t]);  // the MMA may now overwrite S_t with the next scores
+        const int k0 = i * kFKeys;
+        if (k0 + kFKeys - 1 > pos_min) {  // tile crosses the diagonal (warp-uniform)
+#pragma unroll
+          for (int jj = 0; jj < kFKeys; ++jj)
+            if (k0 + jj > pos) sv[jj] = -INFINITY;
         }
-        tmem_wait_st();
-      }
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {  // 8 keys per 16-byte chunk
-        uint4 v;
-        v.x = pack_bf16(sv[8 * c + 0], sv[8 * c + 1]);
-        v.y = pack_bf16(sv[8 * c + 2], sv[8 * c + 3]);
-        v.z = pack_bf16(sv[8 * c + 4], sv[8 * c + 5]);
-        v.w = pack_bf16(sv[8 * c + 6], sv[8 * c + 7]);
-        *reinterpret_cast<uint4*>(sm.p[t][c >> 3] + swz128(r, c & 7)) = v;
+        for (int jj = 0; jj < kFKeys; jj += 4) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) mx[u] = fmaxf(mx[u], sv[jj + u]);
+        }
+        // m: the row's reference maximum (raw score); it moves to the tile's
+        // maximum only when that exceeds it by more than 8 / scale_log2.
+        const float m_tile = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        const float m_new = (m_tile - m) * scale_log2 > kFRescaleLog2 ? m_tile : m;  // m = -inf: moves
+        const float msc = (m_new == -INFINITY ? 0.f : m_new) * scale_log2;
+        const float alpha = m_new == m ? 1.f : fast_exp2(fmaf(m, scale_log2, -msc));  // m = -inf: 0
+        float rs[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int jj = 0; jj < kFKeys; jj += 4) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            sv[jj + u] = fast_exp2(fmaf(sv[jj + u], scale_log2, -msc));
+            rs[u] += sv[jj + u];
+          }
+        }
+        l = l * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+        m = m_new;
+        // This tile's previous P.V must be done: it reads this tile's P
+        // buffer and updates O, which a rescale reads below.
+        if (i > 0) {
+          if (!mbar_wait(&sm.pv_done[t], (npd++) & 1, err, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {  // tcgen05.ld/st are warp-wide
+#pragma unroll 1
+          for (int c = 0; c < kFD / 16; ++c) {
+            float ov[16];
+            tmem_ld16(tO + lane_off + 16 * c, ov);
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) ov[jj] *= alpha;
+            tmem_st16(tO + lane_off + 16 * c, ov);
+          }
+          tmem_wait_st();
+        }
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {  // 8 keys per 16-byte chunk
+          uint4 v;
+          v.x = pack_bf16(sv[8 * c + 0], sv[8 * c + 1]);
+          v.y = pack_bf16(sv[8 * c + 2], sv[8 * c + 3]);
+          v.z = pack_bf16(sv[8 * c + 4], sv[8 * c + 5]);
+          v.w = pack_bf16(sv[8 * c + 6], sv[8 * c + 7]);
+          *reinterpret_cast<uint4*>(sm.p[t][c >> 3] + swz128(r, c & 7)) = v;
+        }
+        fence_proxy_async();
+        tc_fence_before();
+        mbar_arrive(&sm.p_full[t]);
       }
-      fence_proxy_async();
-      tc_fence_before();
-      mbar_arrive(&sm.p_full[t]);
-    }
-    // ---------------- epilogue: O / l ----------------
-    if (ok && ntiles > 0 && mbar_wait(&sm.pv_done[t], (ntiles - 1) & 1, err, abort)) {
+      if (!ok) break;
+      // ---------------- item epilogue: O / l, then O's TMEM is free ----------------
+      if (!mbar_wait(&sm.pv_done[t], (npd++) & 1, err, abort)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       const float il = l > 0.f ? 1.f / l : 0.f;
-      const int g = r % G;
-      bf16* dst = out + ((q0 + qs + p) * Hq + (int64_t)kvh * G + g) * kFD;
 #pragma unroll 1
       for (int c = 0; c < kFD / 16; ++c) {
         float ov[16];
         tmem_ld16(tO + lane_off + 16 * c, ov);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) ov[j] *= il;
+        for (int jj = 0; jj < 16; ++jj) ov[jj] *= il;
         if (row_valid) store16_bf16(dst + 16 * c, ov);
       }
+      tc_fence_before();
+      mbar_arrive(&sm.o_free[t]);
     }
   }
 
@@ -415,15 +474,17 @@ int aacc_prefill_attention(const void* q, void* out, int64_t num_tokens, const v
   st = make_tmap_3d(&tmq, q, kFD, num_q_heads, num_tokens, kFD * 2, (uint64_t)num_q_heads * kFD * 2, 64, G, P, true);
   if (st) return st;
   const int n_pairs = (int)((max_q_len + 2 * P - 1) / (2 * P));
+  const int64_t n_items = (int64_t)n_pairs * num_kv_heads * num_seqs;
+  if (n_items >= (int64_t(1) << 31)) return set_error(AACC_ERR_UNSUPPORTED, "prefill_attention: too many work items");
   const size_t smem = sizeof(FlashSmem) + 1024;
-  dim3 grid(n_pairs, num_kv_heads, (unsigned)num_seqs);
+  dim3 grid((unsigned)std::min<int64_t>(n_items, sm_count()));
   cudaError_t le;
 #define AACC_LAUNCH_FLASH(GG)                                                                                      \
   {                                                                                                                \
     set_smem_once<flash_prefill_kernel<GG>>((int)smem);                                                            \
     le = launch_k(flash_prefill_kernel<GG>, grid, dim3(kFThreads), smem, stream, tmk, tmv, tmq,                    \
                   (bf16*)out, block_tables, max_blocks, seq_rows, cu_q, ctx_start, num_q_heads, num_kv_heads,       \
-                  block_size, num_blocks, n_pairs, scale * kLog2e, device_error_ptr());                            \
+                  block_size, num_blocks, n_pairs, (int)num_seqs, scale * kLog2e, device_error_ptr());             \
   }
   switch (G) {
     case 1: AACC_LAUNCH_FLASH(1) break;
