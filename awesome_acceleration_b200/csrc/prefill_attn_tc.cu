@@ -15,12 +15,12 @@
 //                   slots, K one tile ahead of V (K0 K1 V0 K2 V1 K3 V2 ...):
 //                   a K slot is free once both tiles' S used it, a V slot
 //                   once both P.V did;
-//   MMA warp        S_t(i+1) = Q_t K_{i+1}^T into tile t's TMEM score columns
-//                   as soon as tile t's softmax group has read S_t(i) into
-//                   registers (so it runs under that group's exponentials),
-//                   and O_t += P_t(i) V_i into its TMEM accumulator once the
-//                   group has written P (V read as an MN-major operand, in
-//                   place): S_A' S_B' PV_A PV_B per key tile;
+//   MMA warps       one issuing thread per tile: S_t(i+1) = Q_t K_{i+1}^T
+//                   into tile t's TMEM score columns as soon as tile t's
+//                   softmax group has read S_t(i) into registers (so it runs
+//                   under that group's exponentials), and O_t += P_t(i) V_i
+//                   into its TMEM accumulator once the group has written P
+//                   (V read as an MN-major operand, in place);
 //   softmax groups  4 warps per tile, one thread per row: S from TMEM, causal
 //                   mask key_pos <= query_pos (query p of the chunk sits at
 //                   ctx_start + tile start + p) on the tiles that cross the
@@ -51,7 +51,7 @@ constexpr int kFKeys = 128;         // keys per K/V tile
 constexpr int kFSlots = 3;          // K/V ring: 32 KB slots holding K0 V0 K1 V1 ...
 constexpr int kFGroupWarps = 4;     // one softmax group: a thread per MMA row of one query tile
 constexpr int kFSoftmaxWarps = 2 * kFGroupWarps;
-constexpr int kFThreads = (kFSoftmaxWarps + 2) * 32;
+constexpr int kFThreads = (kFSoftmaxWarps + 3) * 32;  // + producer, + one MMA issuer per tile
 constexpr int kFHalf = 128 * 128;   // bytes of one 64-column half of a 128-row bf16 tile
 constexpr float kFRescaleLog2 = 8.f;  // move a row's reference maximum when exp2 would exceed 2^8
 
@@ -115,7 +115,26 @@ __device__ __forceinline__ bool flash_item(int j, int n_pairs, int Hkv, int n_se
   return true;
 }
 
-// Persistent: one CTA per SM walks items j = blockIdx.x, + gridDim.x, ...;
+// The items of this CTA in snake order: round r takes item r * gridDim.x + k
+// with k = blockIdx.x on even rounds and gridDim.x - 1 - blockIdx.x on odd
+// ones, which evens out the heaviest-first sequence across CTAs.
+template <int P>
+struct FlashItems {
+  int r = 0;
+  __device__ __forceinline__ bool next(FlashItem& it, int n_items, int n_pairs, int Hkv, int n_seqs,
+                                       const int32_t* cu_q, const int32_t* ctx_start, const int64_t* seq_rows,
+                                       int64_t kv_cap) {
+    const int G = gridDim.x, k = blockIdx.x;
+    while (r * G < n_items) {
+      const int j = r * G + ((r & 1) ? G - 1 - k : k);
+      ++r;
+      if (j < n_items && flash_item<P>(j, n_pairs, Hkv, n_seqs, cu_q, ctx_start, seq_rows, kv_cap, it)) return true;
+    }
+    return false;
+  }
+};
+
+// Persistent: one CTA per SM walks its items (FlashItems);
 // barriers and TMEM are set up once, and every barrier's phase runs on across
 // items, so an item's loads and first S start while the previous item's
 // softmax groups finish and store O.
@@ -137,10 +156,10 @@ __global__ void __launch_bounds__(kFThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < kFSlots; ++i) {
       mbar_init(&sm.full[i], 1);
-      mbar_init(&sm.empty[i], 1);
+      mbar_init(&sm.empty[i], 2);  // one arrival per tile's MMA issuer
     }
     mbar_init(&sm.q_full, 1);
-    mbar_init(&sm.q_free, 1);
+    mbar_init(&sm.q_free, 2);
     for (int t = 0; t < 2; ++t) {
       mbar_init(&sm.s_full[t], 1);
       mbar_init(&sm.s_free[t], kFGroupWarps * 32);
@@ -171,9 +190,9 @@ __global__ void __launch_bounds__(kFThreads, 1)
       tma_prefetch_desc(&tmv);
       int U = 0, nq = 0;  // K/V units issued, items whose Q was loaded (running over items)
       bool ok = true;
-      for (int j = blockIdx.x; ok && j < n_items; j += gridDim.x) {
-        FlashItem it;
-        if (!flash_item<P>(j, n_pairs, Hkv, n_seqs, cu_q, ctx_start, seq_rows, kv_cap, it)) continue;
+      FlashItems<P> items;
+      FlashItem it;
+      while (ok && items.next(it, n_items, n_pairs, Hkv, n_seqs, cu_q, ctx_start, seq_rows, kv_cap)) {
         if (it.clamped) report(err, ERR_CTX_OOB);
         // Q tiles (K-major, 128-byte swizzle; row = position * G + head), once
         // the previous item's last S has read the buffers.  Rows past the
@@ -213,13 +232,17 @@ __global__ void __launch_bounds__(kFThreads, 1)
         mbar_wait(&sm.full[sl], (last / kFSlots) & 1, err, nullptr);
       }
     }
-  } else if (warp == kFSoftmaxWarps + 1) {
-    // ---------------- MMA issuer ----------------
-    // Per item: S_A(0) S_B(0); per key tile i: S_A(i+1) S_B(i+1) (each once
-    // its group has read S(i)) then PV_A(i) PV_B(i) (each once its group has
-    // written P(i); the item's first PV also once the group has read the
-    // previous item's O).  Tile B's positions follow tile A's, so B uses every
-    // key tile A uses (nt_b >= nt_a).
+  } else if (warp > kFSoftmaxWarps) {
+    // ---------------- MMA issuers: warp 9 for tile A, warp 10 for tile B ----------------
+    // Each walks its item's K/V units in ring order -- K_0 K_1 V_0 K_2 V_1 ...
+    // V_{nkv-1}, which is also its issue order S(0) S(1) PV(0) S(2) PV(1) ... --
+    // issuing S_t(j) for K_j (once its group has read the previous scores)
+    // and PV_t(j) for V_j (once its group has written P(j); the item's first
+    // PV also once the group has read the previous item's O), and releasing
+    // every unit on the ring's two-arrival empty barrier, with a plain
+    // arrival for units its tile does not use.  The two tiles never wait for
+    // each other.
+    const int t = warp - kFSoftmaxWarps - 1;
     if (lane == 0) {
       constexpr uint32_t id_s = umma_idesc_m128(kFKeys, false);  // S = Q K^T: both K-major (over dims)
       constexpr uint32_t id_pv = umma_idesc_m128(kFD, true);     // O += P V: V is N(dims)-major
@@ -228,74 +251,51 @@ __global__ void __launch_bounds__(kFThreads, 1)
         tc_fence_after();
         return true;
       };
-      auto issue_s = [&](int t, int u) {
-        const uint32_t qb = smem_u32(sm.q[t][0]), kb = smem_u32(sm.kv[u % kFSlots][0]);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {  // 16 dims per step
-          const uint32_t off = (uint32_t)((kk >> 2) * kFHalf + (kk & 3) * 32);
-          umma_bf16(tmem + 128 * t, umma_desc_sw128(qb + off), umma_desc_sw128(kb + off), id_s, kk != 0);
-        }
-        umma_commit(&sm.s_full[t]);
-      };
-      auto issue_pv = [&](int t, int i, int u) {
-        const uint32_t pb = smem_u32(sm.p[t][0]), vb = smem_u32(sm.kv[u % kFSlots][0]);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {  // 16 keys per step
-          const uint64_t a = umma_desc_sw128(pb + (uint32_t)((kk >> 2) * kFHalf + (kk & 3) * 32));
-          const uint64_t b = umma_desc_sw128_mn(vb + (uint32_t)(kk * 16 * 128), kFHalf);
-          umma_bf16(tmem + 256 + 128 * t, a, b, id_pv, (i | kk) != 0);
-        }
-        umma_commit(&sm.pv_done[t]);
-      };
-      // running counts: units consumed, items, and waits per tile on s_free / p_full / o_free
-      int V = 0, nq = 0, nsf[2] = {0, 0}, npf[2] = {0, 0}, nof[2] = {0, 0}, seen[2] = {0, 0};
+      const uint32_t qb = smem_u32(sm.q[t][0]), pb = smem_u32(sm.p[t][0]);
+      const uint32_t tS = tmem + 128 * t, tO = tmem + 256 + 128 * t;
+      // running counts over items: units, items, waits on s_free / p_full / o_free, items with this tile
+      int V = 0, nq = 0, nsf = 0, npf = 0, nof = 0, seen = 0;
       bool ok = true;
-      for (int j = blockIdx.x; ok && j < n_items; j += gridDim.x) {
-        FlashItem it;
-        if (!flash_item<P>(j, n_pairs, Hkv, n_seqs, cu_q, ctx_start, seq_rows, kv_cap, it)) continue;
-        const int nkv = it.nkv, nt_a = it.nt_a, nt_b = it.nt_b;
-        const bool have_b = it.have_b;
+      FlashItems<P> items;
+      FlashItem it;
+      while (ok && items.next(it, n_items, n_pairs, Hkv, n_seqs, cu_q, ctx_start, seq_rows, kv_cap)) {
+        const int nkv = it.nkv, nt = t ? it.nt_b : it.nt_a;  // nt_b = 0 when the item has no tile B
         if (!(ok = wait_bar(&sm.q_full, nq++))) break;
-        const int u0 = V++;  // K_0
-        if (!(ok = wait_bar(&sm.full[u0 % kFSlots], u0 / kFSlots))) break;
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          if (t == 1 && !have_b) break;
-          if (seen[t] && !(ok = wait_bar(&sm.s_free[t], nsf[t]++))) break;  // previous item's last S read
-          issue_s(t, u0);
-        }
-        if (!ok) break;
-        if (nkv == 1) umma_commit(&sm.q_free);  // the item's last S: Q may be replaced
-        umma_commit(&sm.empty[u0 % kFSlots]);
-        for (int i = 0; ok && i < nkv; ++i) {
-          if (i + 1 < nkv) {
-            const int uk = V++;  // K_{i+1}
-            if (!(ok = wait_bar(&sm.full[uk % kFSlots], uk / kFSlots))) break;
-            if (i + 1 < nt_a) {
-              if (!(ok = wait_bar(&sm.s_free[0], nsf[0]++))) break;
-              issue_s(0, uk);
-            }
-            if (have_b && i + 1 < nt_b) {
-              if (!(ok = wait_bar(&sm.s_free[1], nsf[1]++))) break;
-              issue_s(1, uk);
-            }
-            if (i + 2 == nkv) umma_commit(&sm.q_free);
-            umma_commit(&sm.empty[uk % kFSlots]);  // K_{i+1} consumed
+        if (nt == 0) mbar_arrive(&sm.q_free);  // this tile reads no Q in this item
+        for (int u = 0; ok && u < 2 * nkv; ++u) {
+          const int w = u - 1;
+          const bool is_v = u > 0 && (w >= 2 * (nkv - 1) || (w & 1));
+          const int j = u == 0 ? 0 : (w >= 2 * (nkv - 1) ? nkv - 1 : (w >> 1) + (is_v ? 0 : 1));
+          const int uu = V++;
+          if (!(ok = wait_bar(&sm.full[uu % kFSlots], uu / kFSlots))) break;
+          if (j >= nt) {
+            mbar_arrive(&sm.empty[uu % kFSlots]);  // a key tile past this tile's diagonal
+            continue;
           }
-          const int uv = V++;  // V_i
-          if (!(ok = wait_bar(&sm.full[uv % kFSlots], uv / kFSlots))) break;
+          const uint32_t kv = smem_u32(sm.kv[uu % kFSlots][0]);
+          if (!is_v) {
+            if ((j > 0 || seen) && !(ok = wait_bar(&sm.s_free[t], nsf++))) break;  // S_t read
 #pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            if (i >= (t ? (have_b ? nt_b : 0) : nt_a)) continue;
-            if (i == 0 && seen[t] && !(ok = wait_bar(&sm.o_free[t], nof[t]++))) break;  // previous O read
-            if (!(ok = wait_bar(&sm.p_full[t], npf[t]++))) break;
-            issue_pv(t, i, uv);
+            for (int kk = 0; kk < 8; ++kk) {  // 16 dims per step
+              const uint32_t off = (uint32_t)((kk >> 2) * kFHalf + (kk & 3) * 32);
+              umma_bf16(tS, umma_desc_sw128(qb + off), umma_desc_sw128(kv + off), id_s, kk != 0);
+            }
+            umma_commit(&sm.s_full[t]);
+            if (j == nt - 1) umma_commit(&sm.q_free);  // this tile's last S of the item
+          } else {
+            if (j == 0 && seen && !(ok = wait_bar(&sm.o_free[t], nof++))) break;  // previous O read
+            if (!(ok = wait_bar(&sm.p_full[t], npf++))) break;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {  // 16 keys per step
+              const uint64_t a = umma_desc_sw128(pb + (uint32_t)((kk >> 2) * kFHalf + (kk & 3) * 32));
+              const uint64_t b = umma_desc_sw128_mn(kv + (uint32_t)(kk * 16 * 128), kFHalf);
+              umma_bf16(tO, a, b, id_pv, (j | kk) != 0);
+            }
+            umma_commit(&sm.pv_done[t]);
           }
-          if (!ok) break;
-          umma_commit(&sm.empty[uv % kFSlots]);  // V_i consumed
+          umma_commit(&sm.empty[uu % kFSlots]);
         }
-        ++seen[0];
-        if (have_b) ++seen[1];
+        if (nt > 0) ++seen;
       }
     }
   } else {
@@ -309,9 +309,9 @@ __global__ void __launch_bounds__(kFThreads, 1)
     const uint32_t tS = tmem + 128 * t, tO = tmem + 256 + 128 * t;
     int nsf = 0, npd = 0;  // waits on s_full / pv_done (running over items)
     bool ok = true;
-    for (int j = blockIdx.x; ok && j < n_items; j += gridDim.x) {
-      FlashItem it;
-      if (!flash_item<P>(j, n_pairs, Hkv, n_seqs, cu_q, ctx_start, seq_rows, kv_cap, it)) continue;
+    FlashItems<P> items;
+    FlashItem it;
+    while (ok && items.next(it, n_items, n_pairs, Hkv, n_seqs, cu_q, ctx_start, seq_rows, kv_cap)) {
       if (t == 1 && !it.have_b) continue;
       const int qs = it.qs0 + t * P, ntiles = t ? it.nt_b : it.nt_a;
       const bool row_valid = p < (t ? it.rows_b : it.rows_a);
@@ -326,8 +326,9 @@ __global__ void __launch_bounds__(kFThreads, 1)
         tc_fence_after();
         float sv[kFKeys];
 #pragma unroll
-        for (int c = 0; c < kFKeys / 32; ++c)
-          tmem_ld32(tS + lane_off + 32 * c, *reinterpret_cast<float(*)[32]>(sv + 32 * c));
+        for (int c = 0; c < kFKeys / 32; ++c) tmem_ld32_async(tS + lane_off + 32 * c, sv + 32 * c);
+        tmem_wait_ld();
+        tmem_pin(sv);
         tc_fence_before();
         mbar_arrive(&sm.s_free[t]);  // the MMA may now overwrite S_t with the next scores
         const int k0 = i * kFKeys;
@@ -401,15 +402,24 @@ __global__ void __launch_bounds__(kFThreads, 1)
       tc_fence_after();
       const float il = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll 1
-      for (int c = 0; c < kFD / 16; ++c) {
-        float ov[16];
-        tmem_ld16(tO + lane_off + 16 * c, ov);
+      for (int h = 0; h < 2; ++h) {  // 64 columns per TMEM round trip
+        float ov[64];
+        tmem_ld32_async(tO + lane_off + 64 * h, ov);
+        tmem_ld32_async(tO + lane_off + 64 * h + 32, ov + 32);
+        tmem_wait_ld();
+        tmem_pin(ov);
+        if (h == 1) {  // O is in registers: the next item's first P.V may overwrite it
+          tc_fence_before();
+          mbar_arrive(&sm.o_free[t]);
+        }
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) ov[jj] *= il;
-        if (row_valid) store16_bf16(dst + 16 * c, ov);
+        for (int c = 0; c < 4; ++c) {
+          float o16[16];
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) o16[jj] = ov[16 * c + jj] * il;
+          if (row_valid) store16_bf16(dst + 64 * h + 16 * c, o16);
+        }
       }
-      tc_fence_before();
-      mbar_arrive(&sm.o_free[t]);
     }
   }
 
