@@ -223,6 +223,9 @@ class Qwen3Runtime:
         self.chunk = prefill_chunk_tokens
         self.cluster_gemm = os.environ.get("AACC_CLUSTER_GEMM", "0") == "1"
         self.skinny_rows = int(os.environ.get("AACC_SKINNY_ROWS", str(K.SKINNY_DEFAULT_ROWS)))
+        # the small-batch GEMMs take output widths in 128-row weight tiles (every Qwen3 shape)
+        if any(n % 128 for n in (hidden, (self.Hq + 2 * self.Hkv) * 128, 2 * self.I)):
+            self.skinny_rows = 0
         self.skinny_fused_rows = int(os.environ.get("AACC_SKINNY_FUSED_ROWS", str(K.SKINNY_FUSED_ROWS)))
         self.device = embed.device
         self.max_context = kv.max_blocks * kv.block_size
