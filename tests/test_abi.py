@@ -65,3 +65,24 @@ def test_noalloc_decode_checks_arguments_before_touching_the_device():
     import torch
     if not torch.cuda.is_available():
         assert call() == 2                           # AACC_ERR_CUDA: valid arguments reach the device lookup
+
+
+def test_small_batch_gemm_and_prefill_attention_validate_arguments_on_the_host():
+    """The small-batch GEMMs and the prefill attention reject shapes they do
+    not take with AACC_ERR_INVALID before any CUDA call (so this runs without
+    a GPU), and a batch of zero rows is a no-op."""
+    lib = _lib.load()
+    sk = lib.aacc_gemm_skinny_splitk
+    assert sk(None, None, None, 65, 1024, 1024, 1, None) == 1     # more than 64 rows
+    assert b"M <= 64" in lib.aacc_last_error()
+    assert sk(None, None, None, 4, 1000, 1024, 1, None) == 1      # N not a multiple of 128
+    assert sk(None, None, None, 4, 1024, 1000, 1, None) == 1      # K not a multiple of 64
+    assert sk(None, None, None, 4, 1024, 1024, 3, None) == 1      # 3 does not divide 16 slabs
+    assert sk(None, None, None, 0, 1024, 1024, 4, None) == 0      # no rows
+    silu = lib.aacc_skinny_silu_mul
+    assert silu(None, None, None, 1, None, None, 4, 3072, 1024, None) == 1  # no counters
+    pa = lib.aacc_prefill_attention
+    common = (None, None, 64, None, 8, None, None, None)  # k, v, blocks, tables, max_blocks, rows, cu_q, ctx
+    assert pa(None, None, 100, *common, 2, 200, 16, 8, 256, 0.088, None) == 1  # max_q_len > num_tokens
+    assert pa(None, None, 100, *common, 2, 50, 16, 6, 256, 0.088, None) == 1   # 16 heads over 6 kv heads
+    assert pa(None, None, 100, *common, 2, 50, 16, 8, 100, 0.088, None) == 1   # block size not a multiple of 64
