@@ -2,7 +2,8 @@
 // TMEM: the B200 form of flash_attn_varlen_func (llm.py:178-184) for a chunk
 // whose K/V are already stored in the paged pool.
 //
-// One CTA per (pair of query tiles, kv head, sequence).  A tile's 128 MMA
+// A work item is a pair of query tiles of one (sequence, kv head); one
+// persistent CTA per SM walks its items (see FlashItems).  A tile's 128 MMA
 // rows are 128 / G query positions times the G query heads that share the kv
 // head (row r = position p * G + head g, P = 128 / G), so every K/V byte is
 // read once per kv head, not once per query head; the two tiles (A: positions
@@ -12,9 +13,8 @@
 //
 //   producer warp   TMA: K and V tiles (two 64-column halves each, 128-byte
 //                   swizzle) from the paged pool into a ring of three 32 KB
-//                   slots, K one tile ahead of V (K0 K1 V0 K2 V1 K3 V2 ...):
-//                   a K slot is free once both tiles' S used it, a V slot
-//                   once both P.V did;
+//                   slots, K one tile ahead of V (K0 K1 V0 K2 V1 K3 V2 ...);
+//                   a slot is free once both tiles' MMA issuers released it;
 //   MMA warps       one issuing thread per tile: S_t(i+1) = Q_t K_{i+1}^T
 //                   into tile t's TMEM score columns as soon as tile t's
 //                   softmax group has read S_t(i) into registers (so it runs
@@ -48,7 +48,7 @@ namespace aacc {
 
 constexpr int kFD = 128;            // head dim
 constexpr int kFKeys = 128;         // keys per K/V tile
-constexpr int kFSlots = 3;          // K/V ring: 32 KB slots holding K0 V0 K1 V1 ...
+constexpr int kFSlots = 3;          // K/V ring: 32 KB slots holding K0 K1 V0 K2 V1 ...
 constexpr int kFGroupWarps = 4;     // one softmax group: a thread per MMA row of one query tile
 constexpr int kFSoftmaxWarps = 2 * kFGroupWarps;
 constexpr int kFThreads = (kFSoftmaxWarps + 3) * 32;  // + producer, + one MMA issuer per tile
