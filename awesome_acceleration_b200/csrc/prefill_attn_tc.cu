@@ -325,8 +325,10 @@ __global__ void __launch_bounds__(kFThreads, 1)
         }
         tc_fence_after();
         float sv[kFKeys];
+        uint32_t srow = tS + lane_off;
+        asm volatile("" : "+r"(srow));
 #pragma unroll
-        for (int c = 0; c < kFKeys / 32; ++c) tmem_ld32_async(tS + lane_off + 32 * c, sv + 32 * c);
+        for (int c = 0; c < kFKeys / 32; ++c) tmem_ld32_async(srow + 32 * c, sv + 32 * c);
         tmem_wait_ld();
         tmem_pin(sv);
         tc_fence_before();
@@ -380,14 +382,21 @@ __global__ void __launch_bounds__(kFThreads, 1)
           }
           tmem_wait_st();
         }
+        {
+          // row base in the tile's P buffer, recomputed per step (kept out of
+          // registers across the loop); 16-byte chunk c of the row lands at
+          // chunk (c ^ row) % 8 of its 64-key half (128-byte swizzle)
+          uint32_t prow = smem_u32(sm.p[t][0]) + (uint32_t)r * 128u;
+          asm volatile("" : "+r"(prow));
+          const uint32_t r7 = (uint32_t)(r & 7);
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {  // 8 keys per 16-byte chunk
-          uint4 v;
-          v.x = pack_bf16(sv[8 * c + 0], sv[8 * c + 1]);
-          v.y = pack_bf16(sv[8 * c + 2], sv[8 * c + 3]);
-          v.z = pack_bf16(sv[8 * c + 4], sv[8 * c + 5]);
-          v.w = pack_bf16(sv[8 * c + 6], sv[8 * c + 7]);
-          *reinterpret_cast<uint4*>(sm.p[t][c >> 3] + swz128(r, c & 7)) = v;
+          for (int c = 0; c < 16; ++c) {  // 8 keys per 16-byte chunk
+            const uint32_t addr = prow + (uint32_t)(c >> 3) * kFHalf + ((((uint32_t)c & 7u) ^ r7) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr),
+                         "r"(pack_bf16(sv[8 * c + 0], sv[8 * c + 1])), "r"(pack_bf16(sv[8 * c + 2], sv[8 * c + 3])),
+                         "r"(pack_bf16(sv[8 * c + 4], sv[8 * c + 5])), "r"(pack_bf16(sv[8 * c + 6], sv[8 * c + 7]))
+                         : "memory");
+          }
         }
         fence_proxy_async();
         tc_fence_before();
