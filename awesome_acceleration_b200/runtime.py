@@ -223,8 +223,7 @@ class Qwen3Runtime:
         self.chunk = prefill_chunk_tokens
         self.cluster_gemm = os.environ.get("AACC_CLUSTER_GEMM", "0") == "1"
         self.skinny_rows = int(os.environ.get("AACC_SKINNY_ROWS", str(K.SKINNY_DEFAULT_ROWS)))
-        # the small-batch GEMMs take output widths in 128-row weight tiles (every Qwen3 shape)
-        if any(n % 128 for n in (hidden, (self.Hq + 2 * self.Hkv) * 128, 2 * self.I)):
+        if not self.skinny_shapes_ok(hidden, self.Hq, self.Hkv, self.I):
             self.skinny_rows = 0
         self.skinny_fused_rows = int(os.environ.get("AACC_SKINNY_FUSED_ROWS", str(K.SKINNY_FUSED_ROWS)))
         self.device = embed.device
@@ -250,6 +249,12 @@ class Qwen3Runtime:
         self.comm.enable_peer_exchange(max_batch, hidden)
 
     # ------------------------------------------------------------------ layers
+    @staticmethod
+    def skinny_shapes_ok(hidden: int, q_heads: int, kv_heads: int, inter: int) -> bool:
+        """The small-batch GEMMs take output widths in whole 128-row weight
+        tiles: true for every Qwen3 shape and TP slice of one."""
+        return not any(n % 128 for n in (hidden, (q_heads + 2 * kv_heads) * 128, 2 * inter))
+
     def _splits(self, M, w, part):
         if part is None:
             return 1
