@@ -73,3 +73,21 @@ def test_gate_up_interleave_groups_of_64():
     for j in range(I // 64):
         assert torch.equal(w[128 * j:128 * j + 64, 0], torch.arange(64 * j, 64 * j + 64).float())
         assert torch.equal(w[128 * j + 64:128 * j + 128, 0], 1000 + torch.arange(64 * j, 64 * j + 64).float())
+
+
+def test_decode_batch_may_hold_every_kv_slot():
+    """A decode step may hold every KV slot: with more than 256 slots (the
+    Qwen3-32B model at TP4 holds ~450 sequences) the runtime's batch
+    capacity is the slot count, so the scheduler can never build a decode
+    batch larger than the buffers and graphs it stages into."""
+    from awesome_acceleration_b200.model.model import Qwen3Config, Qwen3ForCausalLM
+    from oracle.weights import TINY
+    cfg = Qwen3Config(**{k: v for k, v in TINY.as_dict().items() if k in Qwen3Config.__annotations__})
+    with torch.device("meta"):
+        m = Qwen3ForCausalLM(cfg)
+    m = m.to_empty(device="cpu").to(torch.bfloat16)
+    for slots in (3, 256, 300, 450):
+        m.init_kv_cache(slots, 16, torch.device("cpu"), torch.bfloat16, num_blocks=slots)
+        assert m.max_batch == slots
+    m.init_kv_cache(300, 16, torch.device("cpu"), torch.bfloat16, num_blocks=300, max_batch=64)
+    assert m.max_batch == 64
