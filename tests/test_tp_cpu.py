@@ -178,13 +178,16 @@ def _exit_propagates(rank, world):
     assert time.time() - t0 < 60
 
 
-def _engine_protocol(rank, world, n_req, slots, seed):
+def _engine_protocol(rank, world, n_req, slots, seed, capacity=None):
     """LLMTP's own leader / worker loops on CPU ranks, over a stand-in runtime
     that logs every step it is told to run (and joins a Gloo collective at
     each, as the real one joins NCCL): a continuous-batching job with more
     requests than slots, ragged prompts, per-request max_tokens and
     temperatures must take every rank through the same steps, in the same
-    order, and finish every request."""
+    order, and finish every request.  With `capacity` below `slots` the
+    runtime cannot stage a full batch: the leader must fail its requests
+    before it sends the oversized step, and the workers must leave cleanly
+    instead of waiting inside that step's broadcast."""
     import itertools
     import queue
     import random
@@ -210,7 +213,7 @@ def _engine_protocol(rank, world, n_req, slots, seed):
         temp = torch.zeros(slots, dtype=torch.float32)
 
     class RT:
-        max_batch, use_graphs, buf = slots, True, Buf()
+        max_batch, use_graphs, buf = capacity or slots, True, Buf()
         padded_batch = Qwen3Runtime.padded_batch
 
         def load_decode_inputs(self, ids, positions, rows, temperatures=None, seeds=None):
@@ -290,15 +293,29 @@ def _engine_protocol(rank, world, n_req, slots, seed):
         reqs = [([rnd.randrange(1000) for _ in range(rnd.randint(1, 60))], rnd.choice([1, 2, 5, 9, 17, 30]),
                  rnd.choice([0.0, 0.0, 0.7])) for _ in range(n_req)]
         futs = [eng.generate_ids([p], max_tokens=m, temperature=t, ignore_eos=True) for p, m, t in reqs]
-        outs = [f.result(timeout=60)[0] for f in futs]
-        eng.stop()
-        assert [o.generated_tokens for o in outs] == [m for _, m, _ in reqs]
-        assert eng._loop_error is None, eng._loop_error
+        if capacity:
+            errs = []
+            for f in futs:
+                try:
+                    f.result(timeout=60)
+                except ValueError as e:
+                    errs.append(e)
+            eng.stop()
+            assert errs and "max_batch" in str(errs[0]), errs
+            assert isinstance(eng._loop_error, ValueError)
+        else:
+            outs = [f.result(timeout=60)[0] for f in futs]
+            eng.stop()
+            assert [o.generated_tokens for o in outs] == [m for _, m, _ in reqs]
+            assert eng._loop_error is None, eng._loop_error
     else:
         eng.serve_worker()
     logs = [None] * world
     dist.all_gather_object(logs, log, group=D.get_tp_cpu_group())
     assert all(lg == logs[0] for lg in logs), "ranks ran different step sequences"
+    if capacity:
+        assert all(e[0] != "decode" or e[1] <= capacity for e in logs[0])
+        return
     assert any(e[0] == "decode" and e[1] != len([r for r in e[2] if r >= 0]) for e in logs[0])  # padded buckets ran
     if rank == 0:
         assert RT.most_unread == 2  # a step was run ahead while the previous one was read
@@ -370,6 +387,11 @@ def test_dead_worker_raises_instead_of_hanging():
 @pytest.mark.parametrize("world,n_req,slots", [(2, 40, 12), (3, 90, 40)])
 def test_llmtp_leader_worker_protocol(world, n_req, slots):
     res = spawn(world, _engine_protocol, n_req, slots, world * 1000 + n_req)
+    assert all(v is None for v in res.values()), res
+
+
+def test_llmtp_oversized_decode_batch_fails_without_stranding_workers():
+    res = spawn(2, _engine_protocol, 40, 12, 7, 8)
     assert all(v is None for v in res.values()), res
 
 
