@@ -172,10 +172,19 @@ def pick_splits(M: int, N: int, K: int, sms: int = 148, cap: int = 16, max_elems
     return best
 
 
+def _check_partial(partial, splits: int, M: int, N: int, what: str):
+    """The fp32 partial buffer must hold splits * M * N values (the kernels
+    write every one of them; the C ABI cannot see the buffer's size)."""
+    _req(partial, torch.float32, f"{what}: partial")
+    if partial.numel() < splits * M * N:
+        raise ValueError(f"{what}: partial holds {partial.numel()} values, needs {splits} x {M} x {N}")
+
+
 def gemm_splitk(x, w, partial, splits: int):
     """partial [splits, M, N] fp32 <- split-K partial products of x @ w^T."""
     M, K = x.shape
     N = w.shape[0]
+    _check_partial(partial, splits, M, N, "gemm_splitk")
     _lib.check(_lib_().aacc_gemm_splitk(_p(x), _p(w), _p(partial), M, N, K, splits, _stream()), "gemm_splitk")
     return partial
 
@@ -248,6 +257,7 @@ def gemm_skinny_splitk(x, w, partial, splits: int):
     (M <= 64 rows; the weights are the MMA's 128-row operand)."""
     M, K = x.shape
     N = w.shape[0]
+    _check_partial(partial, splits, M, N, "gemm_skinny_splitk")
     _lib.check(_lib_().aacc_gemm_skinny_splitk(_p(x), _p(w), _p(partial), M, N, K, splits, _stream()),
                "gemm_skinny_splitk")
     return partial
@@ -260,6 +270,7 @@ def skinny_qkv_norm_rope_store(x, w_qkv, partial, splits: int, counters, q_norm_
     M, K = x.shape
     nb, hkv, bs, _ = k_cache.shape
     _check_counters(counters, w_qkv.shape[0], "skinny_qkv_norm_rope_store")
+    _check_partial(partial, splits, M, w_qkv.shape[0], "skinny_qkv_norm_rope_store")
     _lib.check(_lib_().aacc_skinny_qkv_norm_rope_store(
         _p(x), _p(w_qkv), _p(partial), splits, _p(counters), _p(q_norm_w), _p(k_norm_w), eps, _p(positions),
         _p(rope_cos_sin), rope_cos_sin.shape[0], _p(slot_mapping), _p(q_out), _p(k_cache), _p(v_cache), nb,
@@ -272,6 +283,7 @@ def skinny_silu_mul(x, w_gate_up, partial, splits: int, counters, out):
     M, K = x.shape
     I = w_gate_up.shape[0] // 2
     _check_counters(counters, 2 * I, "skinny_silu_mul")
+    _check_partial(partial, splits, M, 2 * I, "skinny_silu_mul")
     _lib.check(_lib_().aacc_skinny_silu_mul(_p(x), _p(w_gate_up), _p(partial), splits, _p(counters), _p(out), M, I, K,
                                             _stream()), "skinny_silu_mul")
     return out
